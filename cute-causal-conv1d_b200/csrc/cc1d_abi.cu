@@ -1,0 +1,441 @@
+// extern "C" launchers of libcc1d_b200.so: argument validation, kernel selection,
+// launch geometry.  See include/causal_conv1d_b200.h for the contract.
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "cc1d_launch.h"
+#include "cc1d_update_launch.h"
+
+namespace cc1d {
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<int64_t> g_launches{0};
+
+cc1d_status fail(cc1d_status code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+cc1d_status fail(cc1d_status code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+cc1d_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(CC1D_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+bool is_float(int dt) { return dt == CC1D_FLOAT32 || dt == CC1D_FLOAT16 || dt == CC1D_BFLOAT16; }
+int elem_size(int dt) { return dt == CC1D_FLOAT32 ? 4 : (dt == CC1D_INT64 ? 8 : (dt == CC1D_INT32 ? 4 : 2)); }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int pow2_ceil(int64_t v) {
+  int p = 1;
+  while (p < v && p < (1 << 30)) p <<= 1;
+  return p;
+}
+int log2i(int v) {
+  int s = 0;
+  while ((1 << s) < v) ++s;
+  return s;
+}
+
+// 16-byte packets along dim (channel-last) are legal for this tensor.
+bool packet_ok_channel_last(const cc1d_tensor& t, int64_t dim) {
+  const int vec = 16 / elem_size(t.dtype);
+  return t.stride[1] == 1 && dim % vec == 0 && aligned16(t.data) && t.stride[0] % vec == 0 &&
+         t.stride[2] % vec == 0;
+}
+// 16-byte packets along seqlen (rows) are legal for this tensor.
+bool packet_ok_rows(const cc1d_tensor& t) {
+  const int vec = 16 / elem_size(t.dtype);
+  return t.stride[2] == 1 && aligned16(t.data) && t.stride[0] % vec == 0 && t.stride[1] % vec == 0;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// Resident CTAs per SM for a kernel (cached per device and kernel).
+int blocks_per_sm(const void* kernel, size_t smem) {
+  static std::mutex mu;
+  static struct Entry { int dev; const void* k; size_t smem; int blocks; } entries[256];
+  static int n_entries = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_entries; ++i)
+    if (entries[i].dev == dev && entries[i].k == kernel && entries[i].smem == smem) return entries[i].blocks;
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, smem) != cudaSuccess || blocks < 1) {
+    cudaGetLastError();
+    blocks = 1;
+  }
+  if (n_entries < 256) entries[n_entries++] = Entry{dev, kernel, smem, blocks};
+  return blocks;
+}
+
+const void* kernel_ptr(bool bwd, int dtype, const LaunchShape& ls) {
+  switch (dtype) {
+    case CC1D_FLOAT32: return bwd ? bwd_kernel_ptr_f32(ls) : fwd_kernel_ptr_f32(ls);
+    case CC1D_FLOAT16: return bwd ? bwd_kernel_ptr_f16(ls) : fwd_kernel_ptr_f16(ls);
+    default: return bwd ? bwd_kernel_ptr_bf16(ls) : fwd_kernel_ptr_bf16(ls);
+  }
+}
+
+cudaError_t dispatch(bool bwd, int dtype, const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
+  switch (dtype) {
+    case CC1D_FLOAT32: return bwd ? bwd_f32(a, ls, s) : fwd_f32(a, ls, s);
+    case CC1D_FLOAT16: return bwd ? bwd_f16(a, ls, s) : fwd_f16(a, ls, s);
+    default: return bwd ? bwd_bf16(a, ls, s) : fwd_bf16(a, ls, s);
+  }
+}
+
+// Launch geometry shared by the forward and backward conv kernels.  It depends only on
+// the problem (not on the device) except for the final grid size.
+struct Geometry {
+  LaunchShape ls;
+  ConvArgs a;        // geometry fields only
+  int64_t ntiles;
+  int64_t nslots;    // backward partial slots per channel tile
+  int64_t ncounters; // backward channel tiles
+};
+
+Geometry plan(bool bwd, int64_t B, int64_t D, int64_t L, int width, int layout, bool packet, int es) {
+  Geometry g;
+  std::memset(&g, 0, sizeof(g));
+  g.ls.width = width;
+  g.ls.layout = layout;
+  g.ls.packet = packet;
+  const int vec = packet ? 16 / es : 1;
+  if (layout == kLayoutChannelLast) {
+    const int64_t nv = (D + vec - 1) / vec;
+    const int TX = (int)std::min<int64_t>(32, pow2_ceil(nv));
+    const int TY = kThreads / TX;
+    int64_t chunk = 64;
+    if (bwd) {
+      // keep the partial slots (batch x sequence tiles) moderate
+      while (B * ((((L + chunk - 1) / chunk) + TY - 1) / TY) > 64 && chunk < (1 << 20)) chunk *= 2;
+    }
+    g.a.tx_shift = log2i(TX);
+    g.a.nv = nv;
+    g.a.chunk = chunk;
+    g.a.nbx = (nv + TX - 1) / TX;
+    g.a.nby = (((L + chunk - 1) / chunk) + TY - 1) / TY;
+    g.ntiles = g.a.nbx * g.a.nby * B;
+    g.nslots = g.a.nby * B;
+    g.ncounters = g.a.nbx;
+    g.ls.smem = bwd ? (size_t)kThreads * vec * (width + 1) * sizeof(float) : 0;
+  } else {
+    const int gmin = vec == 1 ? 4 : 1;  // a round must span at least W-1 positions
+    const int G = (int)std::max<int64_t>(gmin, std::min<int64_t>(32, pow2_ceil((L + vec - 1) / vec)));
+    const int DPB = kThreads / G;
+    const int64_t span = (int64_t)G * vec;
+    const int64_t rounds_per_row = (L + span - 1) / span;
+    int64_t rounds = std::min<int64_t>(rounds_per_row, 8);
+    if (rounds < 1) rounds = 1;
+    int64_t nck = (rounds_per_row + rounds - 1) / rounds;
+    if (nck < 1) nck = 1;
+    g.a.g_shift = log2i(G);
+    g.a.rounds = (int)rounds;
+    g.a.chunk = rounds * span;
+    g.a.nck = nck;
+    g.a.nbx = (D + DPB - 1) / DPB;
+    g.ntiles = g.a.nbx * nck * B;
+    g.nslots = nck * B;
+    g.ncounters = g.a.nbx;
+    g.ls.smem = 0;
+  }
+  return g;
+}
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+int64_t bwd_workspace_for(const Geometry& g, int64_t D, int width) {
+  const int64_t part = round_up(g.nslots * D * (width + 1) * (int64_t)sizeof(float), 256);
+  return part + round_up(g.ncounters * (int64_t)sizeof(unsigned int), 256);
+}
+
+cc1d_status check_conv_common(int64_t B, int64_t D, int64_t L, int64_t W, const cc1d_tensor& x,
+                              const cc1d_tensor& weight, const cc1d_tensor& bias, const cc1d_tensor& seq,
+                              const cc1d_tensor& init) {
+  if (B < 0 || D < 0 || L < 0) return fail(CC1D_ERR_VALUE, "batch, dim and seqlen must be >= 0");
+  if (W < 2 || W > 4) return fail(CC1D_ERR_VALUE, "width must be 2, 3, or 4 (got %lld)", (long long)W);
+  if (!is_float(x.dtype)) return fail(CC1D_ERR_TYPE, "x must be float32, float16, or bfloat16");
+  if (!is_float(weight.dtype)) return fail(CC1D_ERR_TYPE, "weight must be float32, float16, or bfloat16");
+  if (bias.data && !is_float(bias.dtype)) return fail(CC1D_ERR_TYPE, "bias must be a float tensor");
+  if (seq.data && seq.dtype != CC1D_INT32) return fail(CC1D_ERR_TYPE, "seq_idx must be int32");
+  if (init.data && !is_float(init.dtype)) return fail(CC1D_ERR_TYPE, "initial_states must be a float tensor");
+  if (B * D * L > 0 && (!x.data || !weight.data)) return fail(CC1D_ERR_VALUE, "x and weight are required");
+  return CC1D_OK;
+}
+
+}  // namespace
+}  // namespace cc1d
+
+using namespace cc1d;
+
+extern "C" {
+
+const char* cc1d_last_error(void) { return g_last_error.c_str(); }
+
+const char* cc1d_status_string(int status) {
+  switch (status) {
+    case CC1D_OK: return "CC1D_OK";
+    case CC1D_ERR_VALUE: return "CC1D_ERR_VALUE";
+    case CC1D_ERR_TYPE: return "CC1D_ERR_TYPE";
+    case CC1D_ERR_NOT_IMPLEMENTED: return "CC1D_ERR_NOT_IMPLEMENTED";
+    case CC1D_ERR_CUDA: return "CC1D_ERR_CUDA";
+    default: return "CC1D_ERR_UNKNOWN";
+  }
+}
+
+int cc1d_abi_version(void) { return CC1D_ABI_VERSION; }
+
+int64_t cc1d_launch_count(void) { return g_launches.load(); }
+
+cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
+  g_last_error.clear();
+  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+  cc1d_status st = check_conv_common(p->batch, p->dim, p->seqlen, p->width, p->x, p->weight, p->bias,
+                                     p->seq_idx, p->initial_states);
+  if (st != CC1D_OK) return st;
+  if (p->out.dtype != p->x.dtype) return fail(CC1D_ERR_TYPE, "out must have x's dtype");
+  if (p->final_states.data && !is_float(p->final_states.dtype))
+    return fail(CC1D_ERR_TYPE, "final_states must be a float tensor");
+  const int64_t B = p->batch, D = p->dim, L = p->seqlen;
+  const int W = (int)p->width;
+  if (B == 0 || D == 0) return CC1D_OK;
+  if (L == 0) {
+    if (p->final_states.data) return fail(CC1D_ERR_VALUE, "seqlen must be > 0 when final_states are requested");
+    return CC1D_OK;
+  }
+  if (!p->out.data) return fail(CC1D_ERR_VALUE, "out is required");
+
+  int layout = kLayoutChannelLast;
+  bool packet = false;
+  if (p->x.stride[1] == 1 && p->out.stride[1] == 1) {
+    packet = packet_ok_channel_last(p->x, D) && packet_ok_channel_last(p->out, D);
+  } else if (p->x.stride[2] == 1 && p->out.stride[2] == 1) {
+    layout = kLayoutRows;
+    packet = packet_ok_rows(p->x) && packet_ok_rows(p->out);
+  }
+  const int es = elem_size(p->x.dtype);
+  Geometry g = plan(false, B, D, L, W, layout, packet, es);
+  ConvArgs& a = g.a;
+  a.batch = B;
+  a.dim = D;
+  a.seqlen = L;
+  a.x = tensor_arg(p->x);
+  a.weight = tensor_arg(p->weight);
+  a.bias = tensor_arg(p->bias);
+  a.seq_idx = tensor_arg(p->seq_idx);
+  a.init = tensor_arg(p->initial_states);
+  a.final_states = tensor_arg(p->final_states);
+  a.out = tensor_arg(p->out);
+  g.ls.silu = p->silu != 0;
+  g.ls.seq = p->seq_idx.data != nullptr;
+  const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, g.ls), g.ls.smem) * sm_count();
+  g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
+  cudaError_t e = dispatch(false, p->x.dtype, a, g.ls, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d forward launch");
+  g_launches.fetch_add(1);
+  return CC1D_OK;
+}
+
+static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* empty) {
+  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+  cc1d_status st = check_conv_common(p->batch, p->dim, p->seqlen, p->width, p->x, p->weight, p->bias,
+                                     p->seq_idx, p->initial_states);
+  if (st != CC1D_OK) return st;
+  if (p->dout.dtype != p->x.dtype || p->dx.dtype != p->x.dtype)
+    return fail(CC1D_ERR_TYPE, "dout and dx must have x's dtype");
+  if (p->dfinal_states.data && !is_float(p->dfinal_states.dtype))
+    return fail(CC1D_ERR_TYPE, "dfinal_states must be a float tensor");
+  if (p->dinitial_states.data && !is_float(p->dinitial_states.dtype))
+    return fail(CC1D_ERR_TYPE, "dinitial_states must be a float tensor");
+  if (p->dinitial_states.data && !p->initial_states.data)
+    return fail(CC1D_ERR_VALUE, "dinitial_states requires initial_states");
+  if (p->bias.data && !p->dbias) return fail(CC1D_ERR_VALUE, "dbias is required when bias is given");
+  const int64_t B = p->batch, D = p->dim, L = p->seqlen;
+  *empty = (B == 0 || D == 0 || L == 0);
+  if (*empty) return CC1D_OK;
+  if (!p->dout.data || !p->dx.data || !p->dweight) return fail(CC1D_ERR_VALUE, "dout, dx and dweight are required");
+  int layout = kLayoutChannelLast;
+  bool packet = false;
+  if (p->x.stride[1] == 1 && p->dout.stride[1] == 1 && p->dx.stride[1] == 1) {
+    packet = packet_ok_channel_last(p->x, D) && packet_ok_channel_last(p->dout, D) &&
+             packet_ok_channel_last(p->dx, D);
+  } else if (p->x.stride[2] == 1 && p->dout.stride[2] == 1 && p->dx.stride[2] == 1) {
+    layout = kLayoutRows;
+    packet = packet_ok_rows(p->x) && packet_ok_rows(p->dout) && packet_ok_rows(p->dx);
+  }
+  *out_g = plan(true, B, D, L, (int)p->width, layout, packet, elem_size(p->x.dtype));
+  return CC1D_OK;
+}
+
+int64_t cc1d_bwd_workspace_bytes(const cc1d_bwd_params* p) {
+  g_last_error.clear();
+  Geometry g;
+  bool empty = false;
+  if (bwd_prepare(p, &g, &empty) != CC1D_OK) return -1;
+  if (empty) return 0;
+  return bwd_workspace_for(g, p->dim, (int)p->width);
+}
+
+cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
+  g_last_error.clear();
+  Geometry g;
+  bool empty = false;
+  cc1d_status st = bwd_prepare(p, &g, &empty);
+  if (st != CC1D_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t B = p->batch, D = p->dim, L = p->seqlen;
+  const int W = (int)p->width;
+  if (empty) {
+    // no positions: the parameter gradients are zero
+    if (B * D == 0 || !p->dweight) return CC1D_OK;
+    cudaError_t e = cudaMemsetAsync(p->dweight, 0, D * W * sizeof(float), s);
+    if (e == cudaSuccess && p->dbias) e = cudaMemsetAsync(p->dbias, 0, D * sizeof(float), s);
+    if (e == cudaSuccess && p->dinitial_states.data) {
+      // only possible with L == 0; dinitial then equals dfinal (not expressible as memset)
+      return fail(CC1D_ERR_VALUE, "seqlen must be > 0 when dinitial_states are requested");
+    }
+    return e == cudaSuccess ? CC1D_OK : cuda_fail(e, "causal_conv1d backward zero fill");
+  }
+  const int64_t need = bwd_workspace_for(g, D, W);
+  if (!p->workspace || p->workspace_bytes < need)
+    return fail(CC1D_ERR_VALUE, "workspace too small: %lld bytes needed", (long long)need);
+  if (!aligned16(p->workspace)) return fail(CC1D_ERR_VALUE, "workspace must be 16-byte aligned");
+  ConvArgs& a = g.a;
+  a.batch = B;
+  a.dim = D;
+  a.seqlen = L;
+  a.x = tensor_arg(p->x);
+  a.weight = tensor_arg(p->weight);
+  a.bias = tensor_arg(p->bias);
+  a.seq_idx = tensor_arg(p->seq_idx);
+  a.init = tensor_arg(p->initial_states);
+  a.dout = tensor_arg(p->dout);
+  a.dfinal = tensor_arg(p->dfinal_states);
+  a.dx = tensor_arg(p->dx);
+  a.dinit = tensor_arg(p->dinitial_states);
+  a.dweight = p->dweight;
+  a.dbias = p->bias.data ? p->dbias : nullptr;
+  char* ws = static_cast<char*>(p->workspace);
+  a.partials = reinterpret_cast<float*>(ws);
+  a.counters = reinterpret_cast<unsigned int*>(ws + round_up(g.nslots * D * (W + 1) * (int64_t)sizeof(float), 256));
+  g.ls.silu = p->silu != 0;
+  g.ls.seq = p->seq_idx.data != nullptr;
+  cudaError_t e = cudaMemsetAsync(a.counters, 0, g.ncounters * sizeof(unsigned int), s);
+  if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward counter reset");
+  const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, g.ls), g.ls.smem) * sm_count();
+  g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
+  e = dispatch(true, p->x.dtype, a, g.ls, s);
+  if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward launch");
+  g_launches.fetch_add(1);
+  return CC1D_OK;
+}
+
+cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
+  g_last_error.clear();
+  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+  const int64_t B = p->batch, D = p->dim, T = p->seqlen, S = p->state_len, W = p->width;
+  if (B < 0 || D < 0 || T < 0 || S < 0 || p->state_batch < 0) return fail(CC1D_ERR_VALUE, "sizes must be >= 0");
+  if (W < 2 || W > 4) return fail(CC1D_ERR_VALUE, "width must be 2, 3, or 4");
+  if (S < W - 1) return fail(CC1D_ERR_VALUE, "conv_state is shorter than the convolution history");
+  if (!is_float(p->x.dtype)) return fail(CC1D_ERR_TYPE, "x must be float32, float16, or bfloat16");
+  if (!is_float(p->weight.dtype)) return fail(CC1D_ERR_TYPE, "weight must be a float tensor");
+  if (p->bias.data && !is_float(p->bias.dtype)) return fail(CC1D_ERR_TYPE, "bias must be a float tensor");
+  if (p->conv_state.dtype != p->x.dtype || p->out.dtype != p->x.dtype)
+    return fail(CC1D_ERR_TYPE, "conv_state and out must have x's dtype");
+  if (p->cache_seqlens.data && p->cache_seqlens.dtype != CC1D_INT32)
+    return fail(CC1D_ERR_TYPE, "cache_seqlens must be int32");
+  if (p->conv_state_indices.data && p->conv_state_indices.dtype != CC1D_INT32)
+    return fail(CC1D_ERR_TYPE, "conv_state_indices must be int32");
+  if (!p->conv_state_indices.data && p->state_batch < B)
+    return fail(CC1D_ERR_VALUE, "conv_state has fewer rows than the batch");
+  if (B == 0 || D == 0 || T == 0) return CC1D_OK;
+  if (!p->x.data || !p->conv_state.data || !p->weight.data || !p->out.data)
+    return fail(CC1D_ERR_VALUE, "x, conv_state, weight and out are required");
+  const int vec = 16 / elem_size(p->x.dtype);
+  auto ok = [&](const cc1d_tensor& t) {
+    return t.stride[1] == 1 && aligned16(t.data) && t.stride[0] % vec == 0 && t.stride[2] % vec == 0;
+  };
+  const bool packet = D % vec == 0 && ok(p->x) && ok(p->out) && ok(p->conv_state);
+  UpdateArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.batch = B;
+  a.dim = D;
+  a.seqlen = T;
+  a.state_len = S;
+  a.x = tensor_arg(p->x);
+  a.state = tensor_arg(p->conv_state);
+  a.weight = tensor_arg(p->weight);
+  a.bias = tensor_arg(p->bias);
+  a.out = tensor_arg(p->out);
+  a.cache_seqlens = static_cast<const int32_t*>(p->cache_seqlens.data);
+  a.cache_stride = p->cache_seqlens.stride[0];
+  a.indices = static_cast<const int32_t*>(p->conv_state_indices.data);
+  a.indices_stride = p->conv_state_indices.stride[0];
+  a.silu = p->silu;
+  const int64_t items = B * ((D + (packet ? vec : 1) - 1) / (packet ? vec : 1));
+  const int64_t blocks = std::min<int64_t>((items + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
+  cudaError_t e = launch_update(p->x.dtype, a, (int)W, packet, dim3((unsigned)std::max<int64_t>(1, blocks)),
+                                static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d update launch");
+  g_launches.fetch_add(1);
+  return CC1D_OK;
+}
+
+cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* p, void* stream) {
+  g_last_error.clear();
+  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+  const int64_t B = p->batch, D = p->dim, S = p->state_len;
+  if (B < 0 || D < 0 || S < 0 || p->total_tokens < 0) return fail(CC1D_ERR_VALUE, "sizes must be >= 0");
+  if (!is_float(p->x.dtype)) return fail(CC1D_ERR_TYPE, "x must be float32, float16, or bfloat16");
+  if (p->states.dtype != p->x.dtype) return fail(CC1D_ERR_TYPE, "states must have x's dtype");
+  if (p->cu_seqlens.dtype != CC1D_INT32 && p->cu_seqlens.dtype != CC1D_INT64)
+    return fail(CC1D_ERR_TYPE, "cu_seqlens must be int32 or int64");
+  if (B == 0 || D == 0 || S == 0) return CC1D_OK;
+  if (!p->x.data || !p->cu_seqlens.data || !p->states.data)
+    return fail(CC1D_ERR_VALUE, "x, cu_seqlens and states are required");
+  const int vec = 16 / elem_size(p->x.dtype);
+  const bool packet = D % vec == 0 && p->x.stride[1] == 1 && p->states.stride[1] == 1 && aligned16(p->x.data) &&
+                      aligned16(p->states.data) && p->x.stride[0] % vec == 0 && p->states.stride[0] % vec == 0 &&
+                      p->states.stride[2] % vec == 0;
+  VarlenArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.batch = B;
+  a.dim = D;
+  a.state_len = S;
+  a.x = tensor_arg(p->x);
+  a.states = tensor_arg(p->states);
+  a.cu = p->cu_seqlens.data;
+  a.cu_stride = p->cu_seqlens.stride[0];
+  a.cu_is_64 = p->cu_seqlens.dtype == CC1D_INT64;
+  const int64_t items = B * S * ((D + (packet ? vec : 1) - 1) / (packet ? vec : 1));
+  const int64_t blocks = std::min<int64_t>((items + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
+  cudaError_t e = launch_varlen_states(p->x.dtype, a, packet, dim3((unsigned)std::max<int64_t>(1, blocks)),
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d varlen states launch");
+  g_launches.fetch_add(1);
+  return CC1D_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,322 @@
+// Forward kernels of the depthwise causal conv1d (sm_100a).
+//
+// Two layouts, both HBM-bound streaming stencils with fp32 accumulation and fused
+// bias + SiLU:
+//
+//  * channel-last x (stride over dim == 1): a thread owns VEC consecutive channels
+//    (one 16-byte packet) of one batch row and walks `chunk` sequence positions in
+//    order, keeping the W-1 previous rows in registers, so every x row is read once
+//    per chunk (plus a W-1 row halo at the chunk start).  A warp covers 32 packets
+//    of one row: 512 contiguous bytes per load and per store.
+//  * (batch, dim, seqlen)-contiguous x: a group of G lanes walks one channel row,
+//    each lane holding VEC consecutive positions (one 16-byte packet); the W-1
+//    element halo comes from the lane to the left with __shfl_up_sync and across
+//    rounds from a carried register copy of the previous round's tail.
+//
+// Both kernels are persistent: the grid is sized to the resident CTA count and each
+// CTA strides over tiles.  Compiled once per element type (CC1D_DT).
+#include "cc1d_common.cuh"
+#include "cc1d_launch.h"
+
+namespace cc1d {
+
+// ------------------------------------------------------------- channel-last
+template <typename T, int W, int VEC, bool SILU, bool SEQ, int U>
+__global__ void __launch_bounds__(kThreads) fwd_channel_last_kernel(const ConvArgs a) {
+  const int TX = 1 << a.tx_shift;
+  const int tx = threadIdx.x & (TX - 1);
+  const int ty = threadIdx.x >> a.tx_shift;
+  const int TY = kThreads >> a.tx_shift;
+  const int64_t L = a.seqlen;
+  const int64_t ntiles = a.nbx * a.nby * a.batch;
+
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    int64_t t = tile;
+    const int64_t bx = t % a.nbx;
+    t /= a.nbx;
+    const int64_t by = t % a.nby;
+    const int64_t b = t / a.nby;
+    const int64_t cv = bx * TX + tx;
+    const int64_t l0 = (by * TY + ty) * a.chunk;
+    if (cv >= a.nv || l0 >= L) continue;
+    const int64_t l1 = min(l0 + a.chunk, L);
+    const int64_t d0 = cv * VEC;
+
+    float wv[W][VEC], bv[VEC];
+    load_params<W, VEC>(a, d0, wv, bv);
+
+    const T* xrow = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1;
+    T* orow = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 * a.out.s1;
+    const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
+
+    // x at positions l0-(W-1) .. l0-1 (initial states or zeros before 0).
+    float xw[W - 1][VEC];
+    int sw[W - 1];
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k) {
+      const int64_t l = l0 - (W - 1) + k;
+      if (l >= 0) {
+        unpack<T, VEC>(ld_packet<T, VEC>(xrow + l * a.x.s2), xw[k]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v)
+          xw[k][v] = a.init.data ? load_any(a.init.data, a.init.dtype,
+                                            b * a.init.s0 + (d0 + v) * a.init.s1 + (W - 1 + l) * a.init.s2)
+                                 : 0.f;
+      }
+      if constexpr (SEQ) sw[k] = l >= 0 ? srow[l * a.seq_idx.s1] : -1;
+    }
+
+    for (int64_t l = l0; l < l1; l += U) {
+      Packet<T, VEC> raw[U];
+      int sq[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (l + u < l1) raw[u] = ld_packet<T, VEC>(xrow + (l + u) * a.x.s2);
+        if constexpr (SEQ) sq[u] = (l + u < l1) ? srow[(l + u) * a.seq_idx.s1] : -1;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (l + u < l1) {
+          float xc[VEC];
+          unpack<T, VEC>(raw[u], xc);
+          float acc[VEC];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            float s = bv[v];
+#pragma unroll
+            for (int w = 0; w < W - 1; ++w) {
+              float xin = xw[w][v];
+              if constexpr (SEQ) xin = (sw[w] == sq[u]) ? xin : 0.f;
+              s = fmaf(wv[w][v], xin, s);
+            }
+            s = fmaf(wv[W - 1][v], xc[v], s);
+            if constexpr (SEQ) s = (sq[u] >= 0) ? s : 0.f;
+            if constexpr (SILU) s = silu_fwd<T>(s);
+            acc[v] = s;
+          }
+          st_packet<T, VEC>(orow + (l + u) * a.out.s2, pack<T, VEC>(acc));
+#pragma unroll
+          for (int k = 0; k < W - 2; ++k) {
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) xw[k][v] = xw[k + 1][v];
+            if constexpr (SEQ) sw[k] = sw[k + 1];
+          }
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) xw[W - 2][v] = xc[v];
+          if constexpr (SEQ) sw[W - 2] = sq[u];
+        }
+      }
+    }
+
+    // The last chunk holds the final W-1 history entries in its window.
+    if (a.final_states.data && l1 == L) {
+#pragma unroll
+      for (int k = 0; k < W - 1; ++k)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v)
+          store_any(a.final_states.data, a.final_states.dtype,
+                    b * a.final_states.s0 + (d0 + v) * a.final_states.s1 + k * a.final_states.s2, xw[k][v]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------- rows
+// Value of element `idx` (0 <= idx < W-1, run-time) of a W-1 register array.
+template <int N, typename V>
+__device__ __forceinline__ V pick(const V (&arr)[N], int idx) {
+  V r = arr[0];
+#pragma unroll
+  for (int q = 1; q < N; ++q) r = (idx == q) ? arr[q] : r;
+  return r;
+}
+
+template <typename T, int W, int VEC, bool SILU, bool SEQ>
+__global__ void __launch_bounds__(kThreads) fwd_row_kernel(const ConvArgs a) {
+  constexpr unsigned FULL = 0xffffffffu;
+  const int G = 1 << a.g_shift;
+  const int gl = threadIdx.x & (G - 1);
+  const int group = threadIdx.x >> a.g_shift;
+  const int DPB = kThreads >> a.g_shift;
+  const int64_t L = a.seqlen;
+  const int64_t span = (int64_t)G * VEC;
+  const int64_t ntiles = a.nbx * a.nck * a.batch;
+
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    int64_t t = tile;
+    const int64_t dtile = t % a.nbx;
+    t /= a.nbx;
+    const int64_t c = t % a.nck;
+    const int64_t b = t / a.nck;
+    const int64_t d = dtile * DPB + group;
+    const bool row_ok = d < a.dim;
+    const int64_t dd = row_ok ? d : 0;
+    const int64_t cs = c * a.chunk;
+    const int64_t ce = min(cs + a.chunk, L);
+
+    const T* xrow = static_cast<const T*>(a.x.data) + b * a.x.s0 + dd * a.x.s1;
+    T* orow = static_cast<T*>(a.out.data) + b * a.out.s0 + dd * a.out.s1;
+    const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
+
+    float wv[W], bias;
+    {
+      float wt[W][1], bt[1];
+      load_params<W, 1>(a, dd, wt, bt);
+#pragma unroll
+      for (int w = 0; w < W; ++w) wv[w] = wt[w][0];
+      bias = bt[0];
+    }
+
+    // carry[j] = x at cs-(W-1)+j ; scarry likewise for seq_idx
+    float carry[W - 1];
+    int scarry[W - 1];
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      const int64_t pos = cs - (W - 1) + j;
+      float v = 0.f;
+      if (row_ok) {
+        if (pos >= 0) v = to_f32(xrow[pos * a.x.s2]);
+        else if (a.init.data)
+          v = load_any(a.init.data, a.init.dtype, b * a.init.s0 + dd * a.init.s1 + (W - 1 + pos) * a.init.s2);
+      }
+      carry[j] = v;
+      if constexpr (SEQ) scarry[j] = (row_ok && pos >= 0) ? srow[pos * a.seq_idx.s1] : -1;
+    }
+
+    for (int r = 0; r < a.rounds; ++r) {
+      const int64_t e0 = cs + r * span + gl * VEC;
+      float xv[VEC];
+      int sv[VEC];
+      if (row_ok && e0 + VEC <= ce) {
+        unpack<T, VEC>(ld_packet<T, VEC>(xrow + e0), xv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) xv[i] = (row_ok && e0 + i < ce) ? to_f32(xrow[e0 + i]) : 0.f;
+      }
+      if constexpr (SEQ) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) sv[i] = (row_ok && e0 + i < ce) ? srow[(e0 + i) * a.seq_idx.s1] : -1;
+      }
+      // xs[q] = x at e0 - (W-1) + q
+      float xs[VEC + W - 1];
+      int ss[VEC + W - 1];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        xs[W - 1 + i] = xv[i];
+        if constexpr (SEQ) ss[W - 1 + i] = sv[i];
+      }
+#pragma unroll
+      for (int k = 1; k < W; ++k) {
+        const int delta = (k + VEC - 1) / VEC;
+        const int slot = delta * VEC - k;
+        float hv = __shfl_up_sync(FULL, xv[slot], delta, G);
+        int hs = 0;
+        if constexpr (SEQ) hs = __shfl_up_sync(FULL, sv[slot], delta, G);
+        if (gl < delta) {
+          const int idx = W - 1 - k + gl * VEC;
+          hv = pick<W - 1>(carry, idx);
+          if constexpr (SEQ) hs = pick<W - 1>(scarry, idx);
+        }
+        xs[W - 1 - k] = hv;
+        if constexpr (SEQ) ss[W - 1 - k] = hs;
+      }
+      float acc[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        float s = bias;
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          float xin = xs[i + w];
+          if constexpr (SEQ) xin = (ss[i + w] == ss[W - 1 + i]) ? xin : 0.f;
+          s = fmaf(wv[w], xin, s);
+        }
+        if constexpr (SEQ) s = (ss[W - 1 + i] >= 0) ? s : 0.f;
+        if constexpr (SILU) s = silu_fwd<T>(s);
+        acc[i] = s;
+      }
+      if (row_ok && e0 + VEC <= ce) {
+        st_packet<T, VEC>(orow + e0, pack<T, VEC>(acc));
+      } else if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i)
+          if (e0 + i < ce) orow[e0 + i] = from_f32<T>(acc[i]);
+      }
+      // carry = last W-1 elements of this round (the round spans >= W-1 elements)
+#pragma unroll
+      for (int j = 0; j < W - 1; ++j) {
+        const int m = W - 1 - j;
+        const int delta = (m + VEC - 1) / VEC;
+        const int slot = delta * VEC - m;
+        carry[j] = __shfl_sync(FULL, xv[slot], G - delta, G);
+        if constexpr (SEQ) scarry[j] = __shfl_sync(FULL, sv[slot], G - delta, G);
+      }
+    }
+
+    // final states: last W-1 entries of [initial | x], reread from memory.
+    if (a.final_states.data && row_ok && c == a.nck - 1 && gl < W - 1) {
+      const int64_t pos = L - (W - 1) + gl;
+      float v = 0.f;
+      if (pos >= 0) v = to_f32(xrow[pos * a.x.s2]);
+      else if (a.init.data)
+        v = load_any(a.init.data, a.init.dtype, b * a.init.s0 + d * a.init.s1 + (W - 1 + pos) * a.init.s2);
+      store_any(a.final_states.data, a.final_states.dtype,
+                b * a.final_states.s0 + d * a.final_states.s1 + gl * a.final_states.s2, v);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- dispatch
+template <typename T, int W, int VEC>
+static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
+  const bool silu = ls.silu, seq = ls.seq;
+  if (ls.layout == kLayoutChannelLast) {
+    constexpr int U = 4;
+#define CC1D_GO(SI, SQ) fwd_channel_last_kernel<T, W, VEC, SI, SQ, U><<<ls.grid, kThreads, 0, s>>>(a)
+    if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
+    else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
+#undef CC1D_GO
+  } else {
+#define CC1D_GO(SI, SQ) fwd_row_kernel<T, W, VEC, SI, SQ><<<ls.grid, kThreads, 0, s>>>(a)
+    if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
+    else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
+#undef CC1D_GO
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_fwd_t(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
+  constexpr int PV = 16 / sizeof(T);
+  switch (ls.width * 2 + (ls.packet ? 1 : 0)) {
+    case 4: return launch_fwd_w<T, 2, 1>(a, ls, s);
+    case 5: return launch_fwd_w<T, 2, PV>(a, ls, s);
+    case 6: return launch_fwd_w<T, 3, 1>(a, ls, s);
+    case 7: return launch_fwd_w<T, 3, PV>(a, ls, s);
+    case 8: return launch_fwd_w<T, 4, 1>(a, ls, s);
+    case 9: return launch_fwd_w<T, 4, PV>(a, ls, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+static const void* fwd_kernel_ptr_t(const LaunchShape& ls) {
+  // Any instantiation of the same family has the same resource footprint class; the
+  // host uses this only for occupancy queries.
+  constexpr int PV = 16 / sizeof(T);
+  if (ls.layout == kLayoutChannelLast) {
+    if (ls.packet) return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, PV, true, false, 4>);
+    return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, 1, true, false, 4>);
+  }
+  if (ls.packet) return reinterpret_cast<const void*>(fwd_row_kernel<T, 4, PV, true, false>);
+  return reinterpret_cast<const void*>(fwd_row_kernel<T, 4, 1, true, false>);
+}
+
+cudaError_t CC1D_DT_NAME(fwd)(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
+  return launch_fwd_t<CC1D_DT_TYPE>(a, ls, s);
+}
+
+const void* CC1D_DT_NAME(fwd_kernel_ptr)(const LaunchShape& ls) {
+  return fwd_kernel_ptr_t<CC1D_DT_TYPE>(ls);
+}
+
+}  // namespace cc1d

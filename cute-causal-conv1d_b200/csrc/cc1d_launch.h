@@ -1,0 +1,54 @@
+// Host-side interface between the C-ABI launchers (cc1d_abi.cu) and the
+// per-element-type kernel translation units.  Each kernel file is compiled once per
+// element type with -DCC1D_DT=<cc1d_dtype>, which names its entry points
+// <name>_f32 / <name>_f16 / <name>_bf16.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "cc1d_common.cuh"
+
+namespace cc1d {
+
+constexpr int kLayoutChannelLast = 0;  // stride over dim == 1
+constexpr int kLayoutRows = 1;         // stride over seqlen == 1
+
+struct LaunchShape {
+  dim3 grid;
+  int width;
+  int layout;
+  bool packet;  // 16-byte packets (alignment checked on the host) vs single elements
+  bool silu;
+  bool seq;
+  size_t smem;
+};
+
+#define CC1D_DECLARE(name)                                                              \
+  cudaError_t name##_f32(const ConvArgs&, const LaunchShape&, cudaStream_t);            \
+  cudaError_t name##_f16(const ConvArgs&, const LaunchShape&, cudaStream_t);            \
+  cudaError_t name##_bf16(const ConvArgs&, const LaunchShape&, cudaStream_t);           \
+  const void* name##_kernel_ptr_f32(const LaunchShape&);                                \
+  const void* name##_kernel_ptr_f16(const LaunchShape&);                                \
+  const void* name##_kernel_ptr_bf16(const LaunchShape&);
+
+CC1D_DECLARE(fwd)
+CC1D_DECLARE(bwd)
+#undef CC1D_DECLARE
+
+}  // namespace cc1d
+
+#ifdef CC1D_DT
+#if CC1D_DT == 0
+#define CC1D_DT_TYPE float
+#define CC1D_DT_SUFFIX f32
+#elif CC1D_DT == 1
+#define CC1D_DT_TYPE __half
+#define CC1D_DT_SUFFIX f16
+#else
+#define CC1D_DT_TYPE __nv_bfloat16
+#define CC1D_DT_SUFFIX bf16
+#endif
+#define CC1D_CAT2(a, b) a##_##b
+#define CC1D_CAT(a, b) CC1D_CAT2(a, b)
+#define CC1D_DT_NAME(name) CC1D_CAT(name, CC1D_DT_SUFFIX)
+#endif

@@ -1,0 +1,170 @@
+// Decode-time state update and varlen state gather (sm_100a).
+//
+// update: one thread per (batch row, VEC channels).  The output window is
+// [state history | x]; outputs read the old state; the state is written after every
+// output of the row is computed, by the same thread, so the in-place shift needs no
+// synchronisation.  With channel-last x and state the VEC channels move as one 16-byte
+// packet (512 contiguous bytes per warp); other layouts use VEC = 1 with the same code.
+//
+// varlen states: one thread per (sequence, state slot, VEC channels), a pure gather
+// of the last state_len tokens of each packed sequence (zero where the sequence is
+// shorter), bit exact.
+#include "cc1d_common.cuh"
+#include "cc1d_update_launch.h"
+
+namespace cc1d {
+
+__device__ __forceinline__ int64_t pos_mod(int64_t v, int64_t m) {
+  int64_t r = v % m;
+  return r < 0 ? r + m : r;
+}
+
+template <typename T, int W, int VEC>
+__global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
+  const int64_t nv = (a.dim + VEC - 1) / VEC;
+  const int64_t total = nv * a.batch;
+  for (int64_t item = (int64_t)blockIdx.x * kThreads + threadIdx.x; item < total;
+       item += (int64_t)gridDim.x * kThreads) {
+    const int64_t cv = item % nv;
+    const int64_t b = item / nv;
+    const int64_t d0 = cv * VEC;
+    const int64_t T_len = a.seqlen;
+    const int64_t S = a.state_len;
+    const int64_t row = a.indices ? (int64_t)a.indices[b * a.indices_stride] : b;
+    const T* xp = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1;
+    T* op = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 * a.out.s1;
+
+    if (row < 0) {  // padded batch row: zero output, state untouched
+      float z[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) z[v] = 0.f;
+      for (int64_t t = 0; t < T_len; ++t) st_packet<T, VEC>(op + t * a.out.s2, pack<T, VEC>(z));
+      continue;
+    }
+    T* sp = static_cast<T*>(a.state.data) + row * a.state.s0 + d0 * a.state.s1;
+    const int64_t cache = a.cache_seqlens ? (int64_t)a.cache_seqlens[b * a.cache_stride] : 0;
+
+    // weights/bias of VEC channels (the ConvArgs-style helper needs the same fields)
+    float wv[W][VEC], bv[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      const int64_t d = d0 + v;
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        wv[w][v] = load_any(a.weight.data, a.weight.dtype, d * a.weight.s0 + w * a.weight.s1);
+      bv[v] = a.bias.data ? load_any(a.bias.data, a.bias.dtype, d * a.bias.s0) : 0.f;
+    }
+
+    // window = the W-1 history entries, then x
+    float hw[W - 1][VEC];
+#pragma unroll
+    for (int i = 0; i < W - 1; ++i) {
+      const int64_t pos = a.cache_seqlens ? pos_mod(cache - (W - 1) + i, S) : S - (W - 1) + i;
+      unpack<T, VEC>(ld_packet<T, VEC>(sp + pos * a.state.s2), hw[i]);
+    }
+    for (int64_t t = 0; t < T_len; ++t) {
+      float xc[VEC];
+      unpack<T, VEC>(ld_packet<T, VEC>(xp + t * a.x.s2), xc);
+      float acc[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        float s = bv[v];
+#pragma unroll
+        for (int w = 0; w < W - 1; ++w) s = fmaf(wv[w][v], hw[w][v], s);
+        s = fmaf(wv[W - 1][v], xc[v], s);
+        if (a.silu) s = silu_fwd<T>(s);
+        acc[v] = s;
+      }
+      st_packet<T, VEC>(op + t * a.out.s2, pack<T, VEC>(acc));
+#pragma unroll
+      for (int k = 0; k < W - 2; ++k)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) hw[k][v] = hw[k + 1][v];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) hw[W - 2][v] = xc[v];
+    }
+
+    // state write (raw copies, bit exact)
+    if (a.cache_seqlens) {
+      for (int64_t t = 0; t < T_len; ++t)  // in order: with seqlen > state_len the last write wins
+        st_packet<T, VEC>(sp + pos_mod(cache + t, S) * a.state.s2, ld_packet<T, VEC>(xp + t * a.x.s2));
+    } else {
+      for (int64_t s = 0; s < S; ++s) {  // ascending: each source is read before it is overwritten
+        const int64_t src = s + T_len;
+        Packet<T, VEC> v = (src < S) ? ld_packet<T, VEC>(sp + src * a.state.s2)
+                                     : ld_packet<T, VEC>(xp + (src - S) * a.x.s2);
+        st_packet<T, VEC>(sp + s * a.state.s2, v);
+      }
+    }
+  }
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kThreads) varlen_states_kernel(const VarlenArgs a) {
+  const int64_t nv = (a.dim + VEC - 1) / VEC;
+  const int64_t total = nv * a.state_len * a.batch;
+  for (int64_t item = (int64_t)blockIdx.x * kThreads + threadIdx.x; item < total;
+       item += (int64_t)gridDim.x * kThreads) {
+    const int64_t cv = item % nv;
+    int64_t r = item / nv;
+    const int64_t s = r % a.state_len;
+    const int64_t b = r / a.state_len;
+    const int64_t begin = a.cu_is_64 ? static_cast<const int64_t*>(a.cu)[b * a.cu_stride]
+                                     : static_cast<const int32_t*>(a.cu)[b * a.cu_stride];
+    const int64_t end = a.cu_is_64 ? static_cast<const int64_t*>(a.cu)[(b + 1) * a.cu_stride]
+                                   : static_cast<const int32_t*>(a.cu)[(b + 1) * a.cu_stride];
+    const int64_t token = end - a.state_len + s;
+    T* dst = static_cast<T*>(a.states.data) + b * a.states.s0 + cv * VEC * a.states.s1 + s * a.states.s2;
+    Packet<T, VEC> v;
+    if (token >= begin) {
+      v = ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + token * a.x.s0 + cv * VEC * a.x.s1);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) v.v[i] = from_f32<T>(0.f);
+    }
+    st_packet<T, VEC>(dst, v);
+  }
+}
+
+template <typename T>
+static cudaError_t launch_update_t(const UpdateArgs& a, int width, bool packet, dim3 grid, cudaStream_t s) {
+  constexpr int PV = 16 / sizeof(T);
+  switch (width * 2 + (packet ? 1 : 0)) {
+    case 4: update_kernel<T, 2, 1><<<grid, kThreads, 0, s>>>(a); break;
+    case 5: update_kernel<T, 2, PV><<<grid, kThreads, 0, s>>>(a); break;
+    case 6: update_kernel<T, 3, 1><<<grid, kThreads, 0, s>>>(a); break;
+    case 7: update_kernel<T, 3, PV><<<grid, kThreads, 0, s>>>(a); break;
+    case 8: update_kernel<T, 4, 1><<<grid, kThreads, 0, s>>>(a); break;
+    case 9: update_kernel<T, 4, PV><<<grid, kThreads, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_varlen_t(const VarlenArgs& a, bool packet, dim3 grid, cudaStream_t s) {
+  constexpr int PV = 16 / sizeof(T);
+  if (packet) varlen_states_kernel<T, PV><<<grid, kThreads, 0, s>>>(a);
+  else varlen_states_kernel<T, 1><<<grid, kThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_update(int dtype, const UpdateArgs& a, int width, bool packet, dim3 grid, cudaStream_t s) {
+  switch (dtype) {
+    case CC1D_FLOAT32: return launch_update_t<float>(a, width, packet, grid, s);
+    case CC1D_FLOAT16: return launch_update_t<__half>(a, width, packet, grid, s);
+    case CC1D_BFLOAT16: return launch_update_t<__nv_bfloat16>(a, width, packet, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_varlen_states(int dtype, const VarlenArgs& a, bool packet, dim3 grid, cudaStream_t s) {
+  switch (dtype) {
+    case CC1D_FLOAT32: return launch_varlen_t<float>(a, packet, grid, s);
+    case CC1D_FLOAT16: return launch_varlen_t<__half>(a, packet, grid, s);
+    case CC1D_BFLOAT16: return launch_varlen_t<__nv_bfloat16>(a, packet, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace cc1d

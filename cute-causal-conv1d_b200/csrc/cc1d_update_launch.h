@@ -1,0 +1,31 @@
+// Argument blocks and host entry points of the update and varlen-state kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "cc1d_common.cuh"
+
+namespace cc1d {
+
+struct UpdateArgs {
+  int64_t batch, dim, seqlen, state_len;
+  TensorArg x, state, weight, bias, out;
+  const int32_t* cache_seqlens;  // nullable
+  int64_t cache_stride;
+  const int32_t* indices;        // nullable
+  int64_t indices_stride;
+  int32_t silu;
+};
+
+struct VarlenArgs {
+  int64_t batch, dim, state_len;
+  TensorArg x, states;  // x: (tokens, dim) strides s0, s1 ; states: (batch, dim, state_len)
+  const void* cu;
+  int64_t cu_stride;
+  int32_t cu_is_64;
+};
+
+cudaError_t launch_update(int dtype, const UpdateArgs& a, int width, bool packet, dim3 grid, cudaStream_t s);
+cudaError_t launch_varlen_states(int dtype, const VarlenArgs& a, bool packet, dim3 grid, cudaStream_t s);
+
+}  // namespace cc1d

@@ -1,0 +1,113 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol declared in
+include/causal_conv1d_b200.h, and its structs match the ctypes mirror byte for byte."""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from causal_conv1d import _abi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "causal_conv1d_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*[\w\s\*]+?\b(cc1d_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_bound_functions():
+    assert declared_functions() == sorted(_abi.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_abi.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_library_metadata_calls():
+    lib = _abi.load_library()
+    assert lib.cc1d_abi_version() == 1
+    assert lib.cc1d_status_string(2) == b"CC1D_ERR_TYPE"
+    assert lib.cc1d_last_error() == b""
+
+
+def test_validation_errors_need_no_gpu():
+    # bad width is rejected on the host before any CUDA call
+    lib = _abi.load_library()
+    p = _abi.FwdParams()
+    p.batch, p.dim, p.seqlen, p.width = 1, 8, 4, 5
+    assert lib.cc1d_fwd_launch(ctypes.byref(p), None) == 1
+    assert b"width" in lib.cc1d_last_error()
+    p.width = 4
+    p.x.dtype = 3  # int32 x
+    assert lib.cc1d_fwd_launch(ctypes.byref(p), None) == 2
+    u = _abi.UpdateParams()
+    u.batch, u.dim, u.seqlen, u.width, u.state_batch, u.state_len = 1, 8, 1, 4, 1, 2
+    assert lib.cc1d_update_launch(ctypes.byref(u), None) == 1  # state_len < width - 1
+    assert b"shorter" in lib.cc1d_last_error()
+    v = _abi.VarlenParams()
+    v.batch, v.dim, v.state_len = 1, 8, 2
+    v.cu_seqlens.dtype = 0  # float cu_seqlens
+    assert lib.cc1d_varlen_states_launch(ctypes.byref(v), None) == 2
+
+
+def test_empty_problem_is_a_no_op():
+    lib = _abi.load_library()
+    p = _abi.FwdParams()
+    p.batch, p.dim, p.seqlen, p.width = 0, 8, 4, 4
+    assert lib.cc1d_fwd_launch(ctypes.byref(p), None) == 0
+    b = _abi.BwdParams()
+    b.batch, b.dim, b.seqlen, b.width = 2, 8, 0, 3
+    assert lib.cc1d_bwd_workspace_bytes(ctypes.byref(b)) == 0
+
+
+C_LAYOUT_PROBE = r"""
+#include <stddef.h>
+#include <stdio.h>
+#include "causal_conv1d_b200.h"
+#define P(T, F) printf(#T "." #F " %zu\n", offsetof(T, F))
+int main(void) {
+  printf("cc1d_tensor %zu\ncc1d_fwd_params %zu\ncc1d_bwd_params %zu\n", sizeof(cc1d_tensor),
+         sizeof(cc1d_fwd_params), sizeof(cc1d_bwd_params));
+  printf("cc1d_update_params %zu\ncc1d_varlen_states_params %zu\n", sizeof(cc1d_update_params),
+         sizeof(cc1d_varlen_states_params));
+  P(cc1d_fwd_params, out); P(cc1d_fwd_params, silu);
+  P(cc1d_bwd_params, dweight); P(cc1d_bwd_params, workspace_bytes); P(cc1d_bwd_params, silu);
+  P(cc1d_update_params, out); P(cc1d_update_params, silu);
+  P(cc1d_varlen_states_params, states);
+  return 0;
+}
+"""
+
+
+def test_struct_layout_matches_ctypes(tmp_path):
+    src = tmp_path / "probe.c"
+    exe = tmp_path / "probe"
+    src.write_text(C_LAYOUT_PROBE)
+    try:
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
+    except (OSError, subprocess.CalledProcessError):
+        pytest.skip("gcc unavailable")
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    got = dict(line.split() for line in out.strip().splitlines())
+    py = {
+        "cc1d_tensor": ctypes.sizeof(_abi.CTensor),
+        "cc1d_fwd_params": ctypes.sizeof(_abi.FwdParams),
+        "cc1d_bwd_params": ctypes.sizeof(_abi.BwdParams),
+        "cc1d_update_params": ctypes.sizeof(_abi.UpdateParams),
+        "cc1d_varlen_states_params": ctypes.sizeof(_abi.VarlenParams),
+        "cc1d_fwd_params.out": _abi.FwdParams.out.offset,
+        "cc1d_fwd_params.silu": _abi.FwdParams.silu.offset,
+        "cc1d_bwd_params.dweight": _abi.BwdParams.dweight.offset,
+        "cc1d_bwd_params.workspace_bytes": _abi.BwdParams.workspace_bytes.offset,
+        "cc1d_bwd_params.silu": _abi.BwdParams.silu.offset,
+        "cc1d_update_params.out": _abi.UpdateParams.out.offset,
+        "cc1d_update_params.silu": _abi.UpdateParams.silu.offset,
+        "cc1d_varlen_states_params.states": _abi.VarlenParams.states.offset,
+    }
+    assert {k: int(v) for k, v in got.items()} == py
