@@ -59,6 +59,13 @@ bool packet_ok_rows(const cc1d_tensor& t) {
   return t.stride[2] == 1 && aligned16(t.data) && t.stride[0] % vec == 0 && t.stride[1] % vec == 0;
 }
 
+// Packets of `bytes` along dim (channel-last) are legal for this tensor.
+bool stream_ok(const cc1d_tensor& t, int64_t dim, int bytes) {
+  const int vec = bytes / elem_size(t.dtype);
+  return t.stride[1] == 1 && dim % vec == 0 && (reinterpret_cast<uintptr_t>(t.data) % bytes) == 0 &&
+         t.stride[0] % vec == 0 && t.stride[2] % vec == 0;
+}
+
 int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -164,6 +171,36 @@ Geometry plan(bool bwd, int64_t B, int64_t D, int64_t L, int width, int layout, 
   return g;
 }
 
+// Streamed channel-last kernels: one wave of threads, each a contiguous row segment.
+// The segment count per channel column fills the resident thread capacity.
+Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_threads) {
+  Geometry g;
+  std::memset(&g, 0, sizeof(g));
+  g.ls.width = width;
+  g.ls.layout = kLayoutStream;
+  g.ls.packet = true;
+  const int vec = (bwd ? 8 : 16) / es;
+  const int64_t nv = D / vec;
+  const int TX = (int)std::min<int64_t>(32, pow2_ceil(nv));
+  const int TY = kThreads / TX;
+  const int64_t min_rows = bwd ? 64 : 32;
+  const int64_t columns = B * nv;
+  int64_t nseg = std::max<int64_t>(1, resident_threads / std::max<int64_t>(1, columns));
+  nseg = std::min<int64_t>(nseg, std::max<int64_t>(1, (L + min_rows - 1) / min_rows));
+  const int64_t seg = (L + nseg - 1) / nseg;
+  nseg = (L + seg - 1) / seg;
+  g.a.tx_shift = log2i(TX);
+  g.a.nv = nv;
+  g.a.chunk = seg;
+  g.a.nbx = (nv + TX - 1) / TX;
+  g.a.nby = (nseg + TY - 1) / TY;
+  g.ntiles = g.a.nbx * g.a.nby * B;
+  g.nslots = g.a.nby * B;
+  g.ncounters = g.a.nbx;
+  g.ls.smem = (size_t)kStreamDepth * kThreads * (bwd ? 16 : 16);
+  return g;
+}
+
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 int64_t bwd_workspace_for(const Geometry& g, int64_t D, int width) {
@@ -229,14 +266,23 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
 
   int layout = kLayoutChannelLast;
   bool packet = false;
-  if (p->x.stride[1] == 1 && p->out.stride[1] == 1) {
-    packet = packet_ok_channel_last(p->x, D) && packet_ok_channel_last(p->out, D);
-  } else if (p->x.stride[2] == 1 && p->out.stride[2] == 1) {
-    layout = kLayoutRows;
-    packet = packet_ok_rows(p->x) && packet_ok_rows(p->out);
-  }
   const int es = elem_size(p->x.dtype);
-  Geometry g = plan(false, B, D, L, W, layout, packet, es);
+  Geometry g;
+  if (stream_ok(p->x, D, 16) && stream_ok(p->out, D, 16)) {
+    LaunchShape probe{};
+    probe.layout = kLayoutStream;
+    const size_t smem = (size_t)kStreamDepth * kThreads * 16;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), smem) * sm_count() * kThreads;
+    g = plan_stream(false, B, D, L, W, es, resident);
+  } else {
+    if (p->x.stride[1] == 1 && p->out.stride[1] == 1) {
+      packet = packet_ok_channel_last(p->x, D) && packet_ok_channel_last(p->out, D);
+    } else if (p->x.stride[2] == 1 && p->out.stride[2] == 1) {
+      layout = kLayoutRows;
+      packet = packet_ok_rows(p->x) && packet_ok_rows(p->out);
+    }
+    g = plan(false, B, D, L, W, layout, packet, es);
+  }
   ConvArgs& a = g.a;
   a.batch = B;
   a.dim = D;
@@ -250,8 +296,12 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
   a.out = tensor_arg(p->out);
   g.ls.silu = p->silu != 0;
   g.ls.seq = p->seq_idx.data != nullptr;
-  const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, g.ls), g.ls.smem) * sm_count();
-  g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
+  if (g.ls.layout == kLayoutStream) {
+    g.ls.grid = dim3((unsigned)g.ntiles);
+  } else {
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, g.ls), g.ls.smem) * sm_count();
+    g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
+  }
   cudaError_t e = dispatch(false, p->x.dtype, a, g.ls, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d forward launch");
   g_launches.fetch_add(1);
@@ -278,6 +328,15 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
   if (!p->dout.data || !p->dx.data || !p->dweight) return fail(CC1D_ERR_VALUE, "dout, dx and dweight are required");
   int layout = kLayoutChannelLast;
   bool packet = false;
+  const int es = elem_size(p->x.dtype);
+  if (stream_ok(p->x, D, 8) && stream_ok(p->dout, D, 8) && stream_ok(p->dx, D, 8)) {
+    LaunchShape probe{};
+    probe.layout = kLayoutStream;
+    const size_t smem = (size_t)kStreamDepth * kThreads * 16;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem) * sm_count() * kThreads;
+    *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
+    return CC1D_OK;
+  }
   if (p->x.stride[1] == 1 && p->dout.stride[1] == 1 && p->dx.stride[1] == 1) {
     packet = packet_ok_channel_last(p->x, D) && packet_ok_channel_last(p->dout, D) &&
              packet_ok_channel_last(p->dx, D);
@@ -285,7 +344,7 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
     layout = kLayoutRows;
     packet = packet_ok_rows(p->x) && packet_ok_rows(p->dout) && packet_ok_rows(p->dx);
   }
-  *out_g = plan(true, B, D, L, (int)p->width, layout, packet, elem_size(p->x.dtype));
+  *out_g = plan(true, B, D, L, (int)p->width, layout, packet, es);
   return CC1D_OK;
 }
 
@@ -344,8 +403,12 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
   g.ls.seq = p->seq_idx.data != nullptr;
   cudaError_t e = cudaMemsetAsync(a.counters, 0, g.ncounters * sizeof(unsigned int), s);
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward counter reset");
-  const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, g.ls), g.ls.smem) * sm_count();
-  g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
+  if (g.ls.layout == kLayoutStream) {
+    g.ls.grid = dim3((unsigned)g.ntiles);
+  } else {
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, g.ls), g.ls.smem) * sm_count();
+    g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
+  }
   e = dispatch(true, p->x.dtype, a, g.ls, s);
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward launch");
   g_launches.fetch_add(1);
@@ -394,8 +457,10 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   a.indices = static_cast<const int32_t*>(p->conv_state_indices.data);
   a.indices_stride = p->conv_state_indices.stride[0];
   a.silu = p->silu;
-  const int64_t items = B * ((D + (packet ? vec : 1) - 1) / (packet ? vec : 1));
-  const int64_t blocks = std::min<int64_t>((items + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
+  a.weight_vec = packet && p->weight.dtype == CC1D_FLOAT32 && p->weight.stride[1] == 1 &&
+                 p->weight.stride[0] == W && aligned16(p->weight.data);
+  const int64_t nv = (D + (packet ? vec : 1) - 1) / (packet ? vec : 1);
+  const int64_t blocks = ((nv + 31) / 32) * ((B + 7) / 8);
   cudaError_t e = launch_update(p->x.dtype, a, (int)W, packet, dim3((unsigned)std::max<int64_t>(1, blocks)),
                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d update launch");

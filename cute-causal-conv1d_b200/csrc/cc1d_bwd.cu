@@ -265,6 +265,198 @@ __global__ void __launch_bounds__(kThreads) bwd_channel_last_kernel(const ConvAr
   }
 }
 
+// ----------------------------------------------------- channel-last, streamed
+// One wave of persistent threads; thread (packet cv, segment) owns VEC channels and
+// positions [l0, l1) of one batch row.  x rows l0-(W-1) .. l1+W-2 and dout rows
+// l0 .. l1+W-2 stream through private cp.async rings (zero-filled outside [0, L)); the
+// walk is the channel-last kernel's: g at row l, dx at row l-(W-1).
+template <typename T, int W, int VEC, bool SILU, bool SEQ, int P>
+__global__ void __launch_bounds__(kThreads) bwd_stream_kernel(const ConvArgs a) {
+  using Pk = Packet<T, VEC>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Pk* xring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
+  Pk* gring = reinterpret_cast<Pk*>(smem_raw) + P * kThreads + threadIdx.x;
+  float* red = reinterpret_cast<float*>(smem_raw);  // reused after the stream drains
+  const int TX = 1 << a.tx_shift;
+  const int tx = threadIdx.x & (TX - 1);
+  const int ty = threadIdx.x >> a.tx_shift;
+  const int TY = kThreads >> a.tx_shift;
+  const int64_t L = a.seqlen;
+  int64_t t = blockIdx.x;
+  const int64_t bx = t % a.nbx;
+  t /= a.nbx;
+  const int64_t by = t % a.nby;
+  const int64_t b = t / a.nby;
+  const int64_t cv = bx * TX + tx;
+  const int64_t l0 = (by * TY + ty) * a.chunk;
+  const bool active = cv < a.nv && l0 < L;
+  const int64_t l1 = min(l0 + a.chunk, L);
+  const int64_t d0 = cv * VEC;
+
+  float dw[W][VEC], db[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) {
+    db[v] = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) dw[w][v] = 0.f;
+  }
+
+  if (active) {
+    float wv[W][VEC], bv[VEC];
+    load_params<W, VEC>(a, d0, wv, bv);
+    const T* xrow = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0;
+    const T* grow = static_cast<const T*>(a.dout.data) + b * a.dout.s0 + d0;
+    T* dxrow = static_cast<T*>(a.dx.data) + b * a.dx.s0 + d0;
+    const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
+    const int64_t lbeg = l0 - (W - 1);
+    const int n = static_cast<int>(min(l1 + (W - 1), L + (W - 1)) - lbeg);
+    auto issue = [&](int j) {
+      const int64_t l = lbeg + j;
+      const bool okx = l >= 0 && l < L;
+      const bool okg = l >= l0 && l < L;
+      cp_async_packet<sizeof(Pk)>(xring + (j % P) * kThreads, xrow + (okx ? l : 0) * a.x.s2, okx);
+      cp_async_packet<sizeof(Pk)>(gring + (j % P) * kThreads, grow + (okg ? l : 0) * a.dout.s2, okg);
+    };
+#pragma unroll
+    for (int j = 0; j < P - 1; ++j) {
+      if (j < n) issue(j);
+      cp_async_commit();
+    }
+    float xw[W - 1][VEC], gw[W - 1][VEC];
+    int sw[W - 1];
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) xw[k][v] = gw[k][v] = 0.f;
+      sw[k] = -1;
+    }
+    const int64_t emit_lo = (l0 == 0 && a.dinit.data) ? -(int64_t)(W - 1) : l0;
+    const int64_t tail0 = L - (W - 1);
+    for (int j = 0; j < n; ++j) {
+      if (j + P - 1 < n) issue(j + P - 1);
+      cp_async_commit();
+      cp_async_wait<P - 1>();
+      const Pk rx = xring[(j % P) * kThreads];
+      const Pk rg = gring[(j % P) * kThreads];
+      const int64_t l = lbeg + j;
+      float xc[VEC], gc[VEC];
+      unpack<T, VEC>(rx, xc);
+      unpack<T, VEC>(rg, gc);
+      if (l < 0 && a.init.data) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v)
+          xc[v] = load_any(a.init.data, a.init.dtype, b * a.init.s0 + (d0 + v) * a.init.s1 + (W - 1 + l) * a.init.s2);
+      }
+      const int scur = (SEQ && l >= 0 && l < L) ? srow[l * a.seq_idx.s1] : -1;
+      if (j >= W - 1) {
+        float g[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          float gv = gc[v];  // zero beyond L (zero-filled stream)
+          if constexpr (SILU) {
+            float p = bv[v];
+#pragma unroll
+            for (int w = 0; w < W - 1; ++w) {
+              float xin = xw[w][v];
+              if constexpr (SEQ) xin = (sw[w] == scur) ? xin : 0.f;
+              p = fmaf(wv[w][v], xin, p);
+            }
+            p = fmaf(wv[W - 1][v], xc[v], p);
+            if constexpr (SEQ) p = (scur >= 0) ? p : 0.f;
+            gv *= silu_grad(p);
+          }
+          if constexpr (SEQ) gv = (scur >= 0) ? gv : 0.f;
+          g[v] = gv;
+        }
+        if (l < l1) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            db[v] += g[v];
+#pragma unroll
+            for (int w = 0; w < W - 1; ++w) {
+              float xin = xw[w][v];
+              if constexpr (SEQ) xin = (sw[w] == scur) ? xin : 0.f;
+              dw[w][v] = fmaf(g[v], xin, dw[w][v]);
+            }
+            dw[W - 1][v] = fmaf(g[v], xc[v], dw[W - 1][v]);
+          }
+        }
+        const int64_t e = l - (W - 1);
+        if (e >= emit_lo) {
+          float dxv[VEC];
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) {
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < W - 1; ++k) {
+              float gk = gw[k][v];
+              if constexpr (SEQ) gk = (sw[0] == sw[k]) ? gk : 0.f;
+              s = fmaf(wv[W - 1 - k][v], gk, s);
+            }
+            {
+              float gk = g[v];
+              if constexpr (SEQ) gk = (sw[0] == scur) ? gk : 0.f;
+              s = fmaf(wv[0][v], gk, s);
+            }
+            if (a.dfinal.data && e >= tail0)
+              s += load_any(a.dfinal.data, a.dfinal.dtype,
+                            b * a.dfinal.s0 + (d0 + v) * a.dfinal.s1 + (e - tail0) * a.dfinal.s2);
+            dxv[v] = s;
+          }
+          if (e >= 0) {
+            st_packet<T, VEC>(dxrow + e * a.dx.s2, pack<T, VEC>(dxv));
+          } else {
+#pragma unroll
+            for (int v = 0; v < VEC; ++v)
+              store_any(a.dinit.data, a.dinit.dtype,
+                        b * a.dinit.s0 + (d0 + v) * a.dinit.s1 + (e + W - 1) * a.dinit.s2, dxv[v]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < W - 2; ++k)
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) gw[k][v] = gw[k + 1][v];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) gw[W - 2][v] = g[v];
+      }
+#pragma unroll
+      for (int k = 0; k < W - 2; ++k) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) xw[k][v] = xw[k + 1][v];
+        sw[k] = sw[k + 1];
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) xw[W - 2][v] = xc[v];
+      sw[W - 2] = scur;
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // the rings are reused as the reduction buffer
+
+  // ---- deterministic dweight / dbias reduction (as in bwd_channel_last_kernel)
+  float* mine = red + (size_t)threadIdx.x * VEC * (W + 1);
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) {
+#pragma unroll
+    for (int w = 0; w < W; ++w) mine[v * (W + 1) + w] = dw[w][v];
+    mine[v * (W + 1) + W] = db[v];
+  }
+  __syncthreads();
+  const int ncol = TX * VEC * (W + 1);
+  const int64_t dbeg = bx * TX * VEC;
+  const int64_t slot = b * a.nby + by;
+  float* dst = a.partials + slot * a.dim * (W + 1) + dbeg * (W + 1);
+  for (int o = threadIdx.x; o < ncol; o += kThreads) {
+    float sum = 0.f;
+    for (int r = 0; r < TY; ++r) sum += red[r * ncol + o];
+    if (dbeg + o / (W + 1) < a.dim) dst[o] = sum;
+  }
+  if (arrive_last(a.counters + bx, (unsigned)(a.nby * a.batch))) {
+    reduce_tile_partials<W>(a, a.nby * a.batch, dbeg, TX * VEC);
+    if (threadIdx.x == 0) a.counters[bx] = 0;
+  }
+}
+
 // ------------------------------------------------------------------- rows
 template <typename T, int W, int VEC, bool SILU, bool SEQ>
 __global__ void __launch_bounds__(kThreads) bwd_row_kernel(const ConvArgs a) {
@@ -525,7 +717,14 @@ __global__ void __launch_bounds__(kThreads) bwd_row_kernel(const ConvArgs a) {
 template <typename T, int W, int VEC>
 static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   const bool silu = ls.silu, seq = ls.seq;
-  if (ls.layout == kLayoutChannelLast) {
+  if (ls.layout == kLayoutStream) {
+    if constexpr (VEC * sizeof(T) == 8) {
+#define CC1D_GO(SI, SQ) bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth><<<ls.grid, kThreads, ls.smem, s>>>(a)
+      if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
+      else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
+#undef CC1D_GO
+    }
+  } else if (ls.layout == kLayoutChannelLast) {
     constexpr int U = 2;
 #define CC1D_GO(SI, SQ) bwd_channel_last_kernel<T, W, VEC, SI, SQ, U><<<ls.grid, kThreads, ls.smem, s>>>(a)
     if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
@@ -543,6 +742,15 @@ static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
 template <typename T>
 static cudaError_t launch_bwd_t(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   constexpr int PV = 16 / sizeof(T);
+  constexpr int SV = 8 / sizeof(T);  // the streamed kernel moves 8-byte packets
+  if (ls.layout == kLayoutStream) {
+    switch (ls.width) {
+      case 2: return launch_bwd_w<T, 2, SV>(a, ls, s);
+      case 3: return launch_bwd_w<T, 3, SV>(a, ls, s);
+      case 4: return launch_bwd_w<T, 4, SV>(a, ls, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (ls.width * 2 + (ls.packet ? 1 : 0)) {
     case 4: return launch_bwd_w<T, 2, 1>(a, ls, s);
     case 5: return launch_bwd_w<T, 2, PV>(a, ls, s);
@@ -557,6 +765,8 @@ static cudaError_t launch_bwd_t(const ConvArgs& a, const LaunchShape& ls, cudaSt
 template <typename T>
 static const void* bwd_kernel_ptr_t(const LaunchShape& ls) {
   constexpr int PV = 16 / sizeof(T);
+  if (ls.layout == kLayoutStream)
+    return reinterpret_cast<const void*>(bwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepth>);
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(bwd_channel_last_kernel<T, 4, PV, true, false, 2>);
     return reinterpret_cast<const void*>(bwd_channel_last_kernel<T, 4, 1, true, false, 2>);

@@ -110,6 +110,27 @@ __device__ __forceinline__ Packet<T, VEC> pack(const float (&f)[VEC]) {
   return r;
 }
 
+// --------------------------------------------------------------- cp.async ring
+// Asynchronous global->shared copy of one packet (Ampere-style LDGSTS, still the
+// cheapest way on sm_100 for a thread to keep many small loads in flight without
+// holding registers).  `valid == false` writes zeros and reads nothing.
+template <int BYTES>
+__device__ __forceinline__ void cp_async_packet(void* smem_dst, const void* gsrc, bool valid) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  const int src_size = valid ? BYTES : 0;
+  if constexpr (BYTES == 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gsrc), "r"(src_size) : "memory");
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;\n" ::"r"(s), "l"(gsrc), "n"(BYTES), "r"(src_size)
+                 : "memory");
+  }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 // ------------------------------------------------------------------------ SiLU
 // Forward SiLU.  16-bit outputs use the single-MUFU identity
 // silu(p) = h * tanh(h) + h with h = p / 2 (sigmoid(p) = (1 + tanh(p/2)) / 2), whose

@@ -121,6 +121,114 @@ __global__ void __launch_bounds__(kThreads) fwd_channel_last_kernel(const ConvAr
   }
 }
 
+// ----------------------------------------------------- channel-last, streamed
+// One wave of persistent threads.  Thread (packet cv, segment) owns VEC channels and
+// the contiguous positions [l0, l1) of one batch row.  Rows stream through a private
+// ring of P shared-memory slots filled with cp.async (zero-filled outside [0, L)), so
+// P-1 rows per thread are in flight without occupying registers; the W-1 rows before
+// l0 enter the same stream first and only fill the register window.
+template <typename T, int W, int VEC, bool SILU, bool SEQ, int P>
+__global__ void __launch_bounds__(kThreads) fwd_stream_kernel(const ConvArgs a) {
+  using Pk = Packet<T, VEC>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Pk* ring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;  // slot s at ring[s * kThreads]
+  const int TX = 1 << a.tx_shift;
+  const int tx = threadIdx.x & (TX - 1);
+  const int ty = threadIdx.x >> a.tx_shift;
+  const int TY = kThreads >> a.tx_shift;
+  const int64_t L = a.seqlen;
+  int64_t t = blockIdx.x;
+  const int64_t bx = t % a.nbx;
+  t /= a.nbx;
+  const int64_t by = t % a.nby;
+  const int64_t b = t / a.nby;
+  const int64_t cv = bx * TX + tx;
+  const int64_t l0 = (by * TY + ty) * a.chunk;
+  if (cv >= a.nv || l0 >= L) return;
+  const int64_t l1 = min(l0 + a.chunk, L);
+  const int64_t d0 = cv * VEC;
+
+  float wv[W][VEC], bv[VEC];
+  load_params<W, VEC>(a, d0, wv, bv);
+  const T* xrow = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0;
+  T* orow = static_cast<T*>(a.out.data) + b * a.out.s0 + d0;
+  const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
+
+  const int64_t lbeg = l0 - (W - 1);  // stream position j <-> row lbeg + j
+  const int n = static_cast<int>(l1 - lbeg);
+  auto issue = [&](int j) {
+    const int64_t l = lbeg + j;
+    const bool ok = l >= 0 && l < L;
+    cp_async_packet<sizeof(Pk)>(ring + (j % P) * kThreads, xrow + (ok ? l : 0) * a.x.s2, ok);
+  };
+#pragma unroll
+  for (int j = 0; j < P - 1; ++j) {
+    if (j < n) issue(j);
+    cp_async_commit();
+  }
+
+  float xw[W - 1][VEC];
+  int sw[W - 1];
+#pragma unroll
+  for (int k = 0; k < W - 1; ++k) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) xw[k][v] = 0.f;
+    sw[k] = -1;
+  }
+  for (int j = 0; j < n; ++j) {
+    if (j + P - 1 < n) issue(j + P - 1);
+    cp_async_commit();
+    cp_async_wait<P - 1>();
+    const Pk raw = ring[(j % P) * kThreads];
+    const int64_t l = lbeg + j;
+    float xc[VEC];
+    unpack<T, VEC>(raw, xc);
+    if (l < 0 && a.init.data) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v)
+        xc[v] = load_any(a.init.data, a.init.dtype, b * a.init.s0 + (d0 + v) * a.init.s1 + (W - 1 + l) * a.init.s2);
+    }
+    const int scur = (SEQ && l >= 0) ? srow[l * a.seq_idx.s1] : -1;
+    if (j >= W - 1) {
+      float acc[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        float s = bv[v];
+#pragma unroll
+        for (int w = 0; w < W - 1; ++w) {
+          float xin = xw[w][v];
+          if constexpr (SEQ) xin = (sw[w] == scur) ? xin : 0.f;
+          s = fmaf(wv[w][v], xin, s);
+        }
+        s = fmaf(wv[W - 1][v], xc[v], s);
+        if constexpr (SEQ) s = (scur >= 0) ? s : 0.f;
+        if constexpr (SILU) s = silu_fwd<T>(s);
+        acc[v] = s;
+      }
+      st_packet<T, VEC>(orow + l * a.out.s2, pack<T, VEC>(acc));
+    }
+#pragma unroll
+    for (int k = 0; k < W - 2; ++k) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) xw[k][v] = xw[k + 1][v];
+      sw[k] = sw[k + 1];
+    }
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) xw[W - 2][v] = xc[v];
+    sw[W - 2] = scur;
+  }
+  cp_async_wait<0>();
+
+  if (a.final_states.data && l1 == L) {
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k)
+#pragma unroll
+      for (int v = 0; v < VEC; ++v)
+        store_any(a.final_states.data, a.final_states.dtype,
+                  b * a.final_states.s0 + (d0 + v) * a.final_states.s1 + k * a.final_states.s2, xw[k][v]);
+  }
+}
+
 // ------------------------------------------------------------------- rows
 // Value of element `idx` (0 <= idx < W-1, run-time) of a W-1 register array.
 template <int N, typename V>
@@ -269,7 +377,14 @@ __global__ void __launch_bounds__(kThreads) fwd_row_kernel(const ConvArgs a) {
 template <typename T, int W, int VEC>
 static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   const bool silu = ls.silu, seq = ls.seq;
-  if (ls.layout == kLayoutChannelLast) {
+  if (ls.layout == kLayoutStream) {
+    if constexpr (VEC * sizeof(T) == 16) {
+#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth><<<ls.grid, kThreads, ls.smem, s>>>(a)
+      if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
+      else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
+#undef CC1D_GO
+    }
+  } else if (ls.layout == kLayoutChannelLast) {
     constexpr int U = 4;
 #define CC1D_GO(SI, SQ) fwd_channel_last_kernel<T, W, VEC, SI, SQ, U><<<ls.grid, kThreads, 0, s>>>(a)
     if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
@@ -303,6 +418,8 @@ static const void* fwd_kernel_ptr_t(const LaunchShape& ls) {
   // Any instantiation of the same family has the same resource footprint class; the
   // host uses this only for occupancy queries.
   constexpr int PV = 16 / sizeof(T);
+  if (ls.layout == kLayoutStream)
+    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, PV, true, false, kStreamDepth>);
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, PV, true, false, 4>);
     return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, 1, true, false, 4>);

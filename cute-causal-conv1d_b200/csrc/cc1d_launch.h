@@ -12,6 +12,8 @@ namespace cc1d {
 
 constexpr int kLayoutChannelLast = 0;  // stride over dim == 1
 constexpr int kLayoutRows = 1;         // stride over seqlen == 1
+constexpr int kLayoutStream = 2;       // channel-last, per-thread cp.async row stream
+constexpr int kStreamDepth = 8;        // rows in flight per thread (ring slots)
 
 struct LaunchShape {
   dim3 grid;

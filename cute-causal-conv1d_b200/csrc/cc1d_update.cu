@@ -21,39 +21,58 @@ __device__ __forceinline__ int64_t pos_mod(int64_t v, int64_t m) {
 
 template <typename T, int W, int VEC>
 __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
+  // CTA tile: 32 channel packets x 8 batch rows, so the 8 warps of a CTA read the same
+  // weights (the second to eighth reads hit L1).
+  const int tx = threadIdx.x & 31;
+  const int ty = threadIdx.x >> 5;
   const int64_t nv = (a.dim + VEC - 1) / VEC;
-  const int64_t total = nv * a.batch;
-  for (int64_t item = (int64_t)blockIdx.x * kThreads + threadIdx.x; item < total;
-       item += (int64_t)gridDim.x * kThreads) {
-    const int64_t cv = item % nv;
-    const int64_t b = item / nv;
+  const int64_t nbx = (nv + 31) / 32;
+  const int64_t cv = (blockIdx.x % nbx) * 32 + tx;
+  const int64_t b = (blockIdx.x / nbx) * 8 + ty;
+  if (cv < nv && b < a.batch) {
     const int64_t d0 = cv * VEC;
     const int64_t T_len = a.seqlen;
     const int64_t S = a.state_len;
-    const int64_t row = a.indices ? (int64_t)a.indices[b * a.indices_stride] : b;
     const T* xp = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1;
     T* op = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 * a.out.s1;
 
+    float wv[W][VEC], bv[VEC];
+    if (a.weight_vec) {  // contiguous fp32 (dim, W): this thread's VEC*W weights are adjacent
+      const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.weight.data) + d0 * W);
+      float flat[VEC * W];
+#pragma unroll
+      for (int q = 0; q < VEC * W / 4; ++q) {
+        const float4 f = __ldg(wp + q);
+        flat[4 * q] = f.x;
+        flat[4 * q + 1] = f.y;
+        flat[4 * q + 2] = f.z;
+        flat[4 * q + 3] = f.w;
+      }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v)
+#pragma unroll
+        for (int w = 0; w < W; ++w) wv[w][v] = flat[v * W + w];
+    } else {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v)
+#pragma unroll
+        for (int w = 0; w < W; ++w)
+          wv[w][v] = load_any(a.weight.data, a.weight.dtype, (d0 + v) * a.weight.s0 + w * a.weight.s1);
+    }
+#pragma unroll
+    for (int v = 0; v < VEC; ++v)
+      bv[v] = a.bias.data ? load_any(a.bias.data, a.bias.dtype, (d0 + v) * a.bias.s0) : 0.f;
+
+    const int64_t row = a.indices ? (int64_t)a.indices[b * a.indices_stride] : b;
     if (row < 0) {  // padded batch row: zero output, state untouched
       float z[VEC];
 #pragma unroll
       for (int v = 0; v < VEC; ++v) z[v] = 0.f;
       for (int64_t t = 0; t < T_len; ++t) st_packet<T, VEC>(op + t * a.out.s2, pack<T, VEC>(z));
-      continue;
+      return;
     }
     T* sp = static_cast<T*>(a.state.data) + row * a.state.s0 + d0 * a.state.s1;
     const int64_t cache = a.cache_seqlens ? (int64_t)a.cache_seqlens[b * a.cache_stride] : 0;
-
-    // weights/bias of VEC channels (the ConvArgs-style helper needs the same fields)
-    float wv[W][VEC], bv[VEC];
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) {
-      const int64_t d = d0 + v;
-#pragma unroll
-      for (int w = 0; w < W; ++w)
-        wv[w][v] = load_any(a.weight.data, a.weight.dtype, d * a.weight.s0 + w * a.weight.s1);
-      bv[v] = a.bias.data ? load_any(a.bias.data, a.bias.dtype, d * a.bias.s0) : 0.f;
-    }
 
     // window = the W-1 history entries, then x
     float hw[W - 1][VEC];

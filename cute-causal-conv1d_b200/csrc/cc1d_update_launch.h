@@ -15,6 +15,7 @@ struct UpdateArgs {
   const int32_t* indices;        // nullable
   int64_t indices_stride;
   int32_t silu;
+  int32_t weight_vec;  // weight is contiguous fp32 (dim, W), 16-byte aligned, and packets are used
 };
 
 struct VarlenArgs {
