@@ -79,7 +79,7 @@ int sm_count() {
 }
 
 // Resident CTAs per SM for a kernel (cached per device and kernel).
-int blocks_per_sm(const void* kernel, size_t smem) {
+int blocks_per_sm(const void* kernel, size_t smem, int threads = kThreads) {
   static std::mutex mu;
   static struct Entry { int dev; const void* k; size_t smem; int blocks; } entries[256];
   static int n_entries = 0;
@@ -89,7 +89,7 @@ int blocks_per_sm(const void* kernel, size_t smem) {
   for (int i = 0; i < n_entries; ++i)
     if (entries[i].dev == dev && entries[i].k == kernel && entries[i].smem == smem) return entries[i].blocks;
   int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, smem) != cudaSuccess || blocks < 1) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, smem) != cudaSuccess || blocks < 1) {
     cudaGetLastError();
     blocks = 1;
   }
@@ -171,9 +171,10 @@ Geometry plan(bool bwd, int64_t B, int64_t D, int64_t L, int width, int layout, 
   return g;
 }
 
-// Streamed channel-last kernels: one wave of threads, each a contiguous row segment.
-// The segment count per channel column fills the resident thread capacity.
-Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_threads) {
+// Streamed channel-last kernels: one wave of CTAs, each thread a contiguous row segment.
+// The segment count per channel column is chosen so the grid fits the resident CTA
+// capacity (no second, partial wave).
+Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_blocks) {
   Geometry g;
   std::memset(&g, 0, sizeof(g));
   g.ls.width = width;
@@ -182,22 +183,22 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   const int vec = (bwd ? 8 : 16) / es;
   const int64_t nv = D / vec;
   const int TX = (int)std::min<int64_t>(32, pow2_ceil(nv));
-  const int TY = kThreads / TX;
+  const int TY = kStreamThreads / TX;
   const int64_t min_rows = bwd ? 64 : 32;
-  const int64_t columns = B * nv;
-  int64_t nseg = std::max<int64_t>(1, resident_threads / std::max<int64_t>(1, columns));
-  nseg = std::min<int64_t>(nseg, std::max<int64_t>(1, (L + min_rows - 1) / min_rows));
-  const int64_t seg = (L + nseg - 1) / nseg;
-  nseg = (L + seg - 1) / seg;
+  const int64_t nbx = (nv + TX - 1) / TX;
+  int64_t nby = std::max<int64_t>(1, resident_blocks / std::max<int64_t>(1, nbx * B));
+  int64_t seg = (L + nby * TY - 1) / (nby * TY);
+  if (seg < min_rows) seg = min_rows;
+  nby = ((L + seg - 1) / seg + TY - 1) / TY;
   g.a.tx_shift = log2i(TX);
   g.a.nv = nv;
   g.a.chunk = seg;
-  g.a.nbx = (nv + TX - 1) / TX;
-  g.a.nby = (nseg + TY - 1) / TY;
-  g.ntiles = g.a.nbx * g.a.nby * B;
-  g.nslots = g.a.nby * B;
-  g.ncounters = g.a.nbx;
-  g.ls.smem = (size_t)kStreamDepth * kThreads * (bwd ? 16 : 16);
+  g.a.nbx = nbx;
+  g.a.nby = nby;
+  g.ntiles = nbx * nby * B;
+  g.nslots = nby * B;
+  g.ncounters = nbx;
+  g.ls.smem = (size_t)kStreamDepth * kStreamThreads * 16;
   return g;
 }
 
@@ -271,8 +272,8 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
   if (stream_ok(p->x, D, 16) && stream_ok(p->out, D, 16)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
-    const size_t smem = (size_t)kStreamDepth * kThreads * 16;
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), smem) * sm_count() * kThreads;
+    const size_t smem = (size_t)kStreamDepth * kStreamThreads * 16;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), smem, kStreamThreads) * sm_count();
     g = plan_stream(false, B, D, L, W, es, resident);
   } else {
     if (p->x.stride[1] == 1 && p->out.stride[1] == 1) {
@@ -332,8 +333,8 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
   if (stream_ok(p->x, D, 8) && stream_ok(p->dout, D, 8) && stream_ok(p->dx, D, 8)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
-    const size_t smem = (size_t)kStreamDepth * kThreads * 16;
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem) * sm_count() * kThreads;
+    const size_t smem = (size_t)kStreamDepth * kStreamThreads * 16;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kStreamThreads) * sm_count();
     *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }

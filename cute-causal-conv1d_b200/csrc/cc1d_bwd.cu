@@ -28,12 +28,12 @@ __device__ __forceinline__ V pick_b(const V (&arr)[N], int idx) {
 // Sums the per-tile partials of one channel tile, in slot order, into dweight/dbias.
 // `nslots` slots of `dim*(W+1)` floats; this CTA's tile covers channels
 // [d_begin, d_begin + nch).
-template <int W>
+template <int W, int NT = kThreads>
 __device__ __forceinline__ void reduce_tile_partials(const ConvArgs& a, int64_t nslots, int64_t d_begin,
                                                      int nch) {
   const int64_t row = a.dim * (W + 1);
   const int n = nch * (W + 1);
-  for (int o = threadIdx.x; o < n; o += kThreads) {
+  for (int o = threadIdx.x; o < n; o += NT) {
     const int64_t d = d_begin + o / (W + 1);
     if (d >= a.dim) continue;
     const int w = o % (W + 1);
@@ -266,21 +266,104 @@ __global__ void __launch_bounds__(kThreads) bwd_channel_last_kernel(const ConvAr
 }
 
 // ----------------------------------------------------- channel-last, streamed
+// Register state of one thread's walk down its row segment (VEC channels as H pairs).
+template <typename T, int W, int VEC, bool SILU, bool SEQ>
+struct BwdWalk {
+  static constexpr int H = VEC / 2;
+  float2 wv[W][H], bv[H];
+  float2 dw[W][H], db[H];
+  float2 xw[W - 1][H], gw[W - 1][H];  // x and g at the W-1 rows before the current one
+  int sw[W - 1];
+
+  // One row: g = dout * silu'(p) at this row; optional dweight/dbias accumulation;
+  // dx of the row W-1 earlier into `dxv`.  Windows advance by one row.
+  template <bool ACC, bool EMIT>
+  __device__ __forceinline__ void step(const float2 (&xc)[H], const float2 (&gc)[H], int scur, bool acc,
+                                       float2 (&dxv)[H]) {
+    float2 g[H];
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      float2 gv = gc[i];
+      if constexpr (SILU) {
+        float2 p = bv[i];
+#pragma unroll
+        for (int w = 0; w < W - 1; ++w) {
+          float2 xin = xw[w][i];
+          if constexpr (SEQ) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
+          p = ffma2(wv[w][i], xin, p);
+        }
+        p = ffma2(wv[W - 1][i], xc[i], p);
+        if constexpr (SEQ) p = (scur >= 0) ? p : make_float2(0.f, 0.f);
+        gv = fmul2(gv, silu_grad2(p));
+      }
+      if constexpr (SEQ) gv = (scur >= 0) ? gv : make_float2(0.f, 0.f);
+      g[i] = gv;
+    }
+    if (ACC && acc) {
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        db[i] = fadd2(db[i], g[i]);
+#pragma unroll
+        for (int w = 0; w < W - 1; ++w) {
+          float2 xin = xw[w][i];
+          if constexpr (SEQ) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
+          dw[w][i] = ffma2(g[i], xin, dw[w][i]);
+        }
+        dw[W - 1][i] = ffma2(g[i], xc[i], dw[W - 1][i]);
+      }
+    }
+    if constexpr (EMIT) {
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < W - 1; ++k) {
+          float2 gk = gw[k][i];
+          if constexpr (SEQ) gk = (sw[0] == sw[k]) ? gk : make_float2(0.f, 0.f);
+          s = ffma2(wv[W - 1 - k][i], gk, s);
+        }
+        float2 gk = g[i];
+        if constexpr (SEQ) gk = (sw[0] == scur) ? gk : make_float2(0.f, 0.f);
+        dxv[i] = ffma2(wv[0][i], gk, s);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < W - 2; ++k) {
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        xw[k][i] = xw[k + 1][i];
+        gw[k][i] = gw[k + 1][i];
+      }
+      sw[k] = sw[k + 1];
+    }
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      xw[W - 2][i] = xc[i];
+      gw[W - 2][i] = g[i];
+    }
+    sw[W - 2] = scur;
+  }
+};
+
 // One wave of persistent threads; thread (packet cv, segment) owns VEC channels and
-// positions [l0, l1) of one batch row.  x rows l0-(W-1) .. l1+W-2 and dout rows
-// l0 .. l1+W-2 stream through private cp.async rings (zero-filled outside [0, L)); the
-// walk is the channel-last kernel's: g at row l, dx at row l-(W-1).
-template <typename T, int W, int VEC, bool SILU, bool SEQ, int P>
-__global__ void __launch_bounds__(kThreads) bwd_stream_kernel(const ConvArgs a) {
+// positions [l0, l1) of one batch row.  The x rows l0-(W-1) .. l0-1 (or initial states)
+// are read once into the window; x and dout rows l0 .. min(l1+W-1, L)-1 stream through
+// private cp.async rings.  Row l produces g[l] (and dweight/dbias terms when l < l1) and
+// dx[l-(W-1)].  The first W-1 rows (which may emit dinitial_states) and the W-1 rows
+// past l1 (dfinal_states, rows past L) run a checked path; the rows in between run an
+// unrolled loop with compile-time ring slots and no checks.
+template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT>
+__global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
   using Pk = Packet<T, VEC>;
+  constexpr int H = VEC / 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Pk* xring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
-  Pk* gring = reinterpret_cast<Pk*>(smem_raw) + P * kThreads + threadIdx.x;
+  Pk* gring = reinterpret_cast<Pk*>(smem_raw) + P * NT + threadIdx.x;
   float* red = reinterpret_cast<float*>(smem_raw);  // reused after the stream drains
   const int TX = 1 << a.tx_shift;
   const int tx = threadIdx.x & (TX - 1);
   const int ty = threadIdx.x >> a.tx_shift;
-  const int TY = kThreads >> a.tx_shift;
+  const int TY = NT >> a.tx_shift;
   const int64_t L = a.seqlen;
   int64_t t = blockIdx.x;
   const int64_t bx = t % a.nbx;
@@ -290,169 +373,182 @@ __global__ void __launch_bounds__(kThreads) bwd_stream_kernel(const ConvArgs a) 
   const int64_t cv = bx * TX + tx;
   const int64_t l0 = (by * TY + ty) * a.chunk;
   const bool active = cv < a.nv && l0 < L;
-  const int64_t l1 = min(l0 + a.chunk, L);
   const int64_t d0 = cv * VEC;
 
-  float dw[W][VEC], db[VEC];
+  BwdWalk<T, W, VEC, SILU, SEQ> st;
 #pragma unroll
-  for (int v = 0; v < VEC; ++v) {
-    db[v] = 0.f;
+  for (int i = 0; i < H; ++i) {
+    st.db[i] = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < W; ++w) dw[w][v] = 0.f;
+    for (int w = 0; w < W; ++w) st.dw[w][i] = make_float2(0.f, 0.f);
   }
 
   if (active) {
-    float wv[W][VEC], bv[VEC];
-    load_params<W, VEC>(a, d0, wv, bv);
-    const T* xrow = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0;
-    const T* grow = static_cast<const T*>(a.dout.data) + b * a.dout.s0 + d0;
-    T* dxrow = static_cast<T*>(a.dx.data) + b * a.dx.s0 + d0;
-    const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
-    const int64_t lbeg = l0 - (W - 1);
-    const int n = static_cast<int>(min(l1 + (W - 1), L + (W - 1)) - lbeg);
-    auto issue = [&](int j) {
-      const int64_t l = lbeg + j;
-      const bool okx = l >= 0 && l < L;
-      const bool okg = l >= l0 && l < L;
-      cp_async_packet<sizeof(Pk)>(xring + (j % P) * kThreads, xrow + (okx ? l : 0) * a.x.s2, okx);
-      cp_async_packet<sizeof(Pk)>(gring + (j % P) * kThreads, grow + (okg ? l : 0) * a.dout.s2, okg);
+    const int64_t l1 = min(l0 + a.chunk, L);
+    const int nmain = static_cast<int>(l1 - l0);                   // rows that accumulate
+    const int nload = static_cast<int>(min(l1 + (W - 1), L) - l0);  // rows with data
+    const int nall = nmain + (W - 1);                                // rows walked
+    const int64_t sx = a.x.s2, sg = a.dout.s2, sd = a.dx.s2;
+    const T* xsrc = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l0 * sx;
+    const T* gsrc = static_cast<const T*>(a.dout.data) + b * a.dout.s0 + d0 + l0 * sg;
+    // stream row j <-> position l0 + j; ring slot j % P
+    auto issue = [&](int j, int slot) {
+      if (j < nload) {
+        cp_async_packet<sizeof(Pk)>(xring + slot * NT, xsrc + j * sx, true);
+        cp_async_packet<sizeof(Pk)>(gring + slot * NT, gsrc + j * sg, true);
+      }
     };
 #pragma unroll
     for (int j = 0; j < P - 1; ++j) {
-      if (j < n) issue(j);
+      issue(j, j);
       cp_async_commit();
     }
-    float xw[W - 1][VEC], gw[W - 1][VEC];
-    int sw[W - 1];
+
+    {
+      float wf[W][VEC], bf[VEC];
+      load_params<W, VEC>(a, d0, wf, bf);
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        st.bv[i] = make_float2(bf[2 * i], bf[2 * i + 1]);
+#pragma unroll
+        for (int w = 0; w < W; ++w) st.wv[w][i] = make_float2(wf[w][2 * i], wf[w][2 * i + 1]);
+      }
+    }
+    const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
 #pragma unroll
     for (int k = 0; k < W - 1; ++k) {
+      const int64_t l = l0 - (W - 1) + k;
+      if (l >= 0) {
+        unpack2<T, VEC>(ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l * sx), st.xw[k]);
+      } else if (a.init.data) {
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) xw[k][v] = gw[k][v] = 0.f;
-      sw[k] = -1;
+        for (int i = 0; i < H; ++i) {
+          const int64_t o = b * a.init.s0 + (d0 + 2 * i) * a.init.s1 + (W - 1 + l) * a.init.s2;
+          st.xw[k][i] = make_float2(load_any(a.init.data, a.init.dtype, o),
+                                    load_any(a.init.data, a.init.dtype, o + a.init.s1));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < H; ++i) st.xw[k][i] = make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < H; ++i) st.gw[k][i] = make_float2(0.f, 0.f);
+      st.sw[k] = (SEQ && l >= 0) ? srow[l * a.seq_idx.s1] : -1;
     }
-    const int64_t emit_lo = (l0 == 0 && a.dinit.data) ? -(int64_t)(W - 1) : l0;
+    T* dxbase = static_cast<T*>(a.dx.data) + b * a.dx.s0 + d0;
     const int64_t tail0 = L - (W - 1);
-    for (int j = 0; j < n; ++j) {
-      if (j + P - 1 < n) issue(j + P - 1);
+    const bool want_dinit = l0 == 0 && a.dinit.data != nullptr;
+
+    // checked row: dx of position e = l-(W-1) goes to dx (e >= l0), to dinitial
+    // (e < 0, first segment), or nowhere; dfinal_states is added on the tail.
+    auto checked_row = [&](int j, int slot) {
+      const int64_t l = l0 + j;
+      float2 xc[H], gc[H];
+      if (j < nload) {
+        unpack2<T, VEC>(xring[slot * NT], xc);
+        unpack2<T, VEC>(gring[slot * NT], gc);
+      } else {
+#pragma unroll
+        for (int i = 0; i < H; ++i) xc[i] = gc[i] = make_float2(0.f, 0.f);
+      }
+      const int scur = (SEQ && j < nload) ? srow[l * a.seq_idx.s1] : -1;
+      const int64_t e = l - (W - 1);
+      float2 dxv[H];
+      st.template step<true, true>(xc, gc, scur, j < nmain, dxv);
+      if (e >= l0 || (e < 0 && want_dinit)) {
+        if (a.dfinal.data && e >= tail0) {
+#pragma unroll
+          for (int i = 0; i < H; ++i) {
+            const int64_t o = b * a.dfinal.s0 + (d0 + 2 * i) * a.dfinal.s1 + (e - tail0) * a.dfinal.s2;
+            dxv[i].x += load_any(a.dfinal.data, a.dfinal.dtype, o);
+            dxv[i].y += load_any(a.dfinal.data, a.dfinal.dtype, o + a.dfinal.s1);
+          }
+        }
+        if (e >= 0) {
+          st_packet<T, VEC>(dxbase + e * sd, pack2<T, VEC>(dxv));
+        } else {
+#pragma unroll
+          for (int i = 0; i < H; ++i) {
+            const int64_t o = b * a.dinit.s0 + (d0 + 2 * i) * a.dinit.s1 + (e + W - 1) * a.dinit.s2;
+            store_any(a.dinit.data, a.dinit.dtype, o, dxv[i].x);
+            store_any(a.dinit.data, a.dinit.dtype, o + a.dinit.s1, dxv[i].y);
+          }
+        }
+      }
+    };
+
+    // head: rows 0 .. W-2
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      if (j < nall) {
+        issue(j + P - 1, (j + P - 1) % P);
+        cp_async_commit();
+        cp_async_wait<P - 1>();
+        checked_row(j, j % P);
+      }
+    }
+    // steady state: rows W-1 .. nmain-1 (full data, accumulate, dx at e >= l0)
+    const int jsteady_end = nmain;
+    const int* sptr = SEQ ? srow + (l0 + W - 1) * a.seq_idx.s1 : nullptr;
+    T* dxptr = dxbase + l0 * sd;
+    for (int j0 = W - 1; j0 < jsteady_end; j0 += P) {
+#pragma unroll
+      for (int u = 0; u < P; ++u) {
+        const int j = j0 + u;
+        if (j < jsteady_end) {
+          issue(j + P - 1, (u + W - 1 + P - 1) % P);
+          cp_async_commit();
+          cp_async_wait<P - 1>();
+          float2 xc[H], gc[H];
+          unpack2<T, VEC>(xring[((u + W - 1) % P) * NT], xc);
+          unpack2<T, VEC>(gring[((u + W - 1) % P) * NT], gc);
+          int scur = 0;
+          if constexpr (SEQ) {
+            scur = *sptr;
+            sptr += a.seq_idx.s1;
+          }
+          float2 dxv[H];
+          st.template step<true, true>(xc, gc, scur, true, dxv);
+          st_packet<T, VEC>(dxptr, pack2<T, VEC>(dxv));
+          dxptr += sd;
+        }
+      }
+    }
+    // tail: rows max(W-1, nmain) .. nall-1
+    for (int j = max(W - 1, nmain); j < nall; ++j) {
+      issue(j + P - 1, (j + P - 1) % P);
       cp_async_commit();
       cp_async_wait<P - 1>();
-      const Pk rx = xring[(j % P) * kThreads];
-      const Pk rg = gring[(j % P) * kThreads];
-      const int64_t l = lbeg + j;
-      float xc[VEC], gc[VEC];
-      unpack<T, VEC>(rx, xc);
-      unpack<T, VEC>(rg, gc);
-      if (l < 0 && a.init.data) {
-#pragma unroll
-        for (int v = 0; v < VEC; ++v)
-          xc[v] = load_any(a.init.data, a.init.dtype, b * a.init.s0 + (d0 + v) * a.init.s1 + (W - 1 + l) * a.init.s2);
-      }
-      const int scur = (SEQ && l >= 0 && l < L) ? srow[l * a.seq_idx.s1] : -1;
-      if (j >= W - 1) {
-        float g[VEC];
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-          float gv = gc[v];  // zero beyond L (zero-filled stream)
-          if constexpr (SILU) {
-            float p = bv[v];
-#pragma unroll
-            for (int w = 0; w < W - 1; ++w) {
-              float xin = xw[w][v];
-              if constexpr (SEQ) xin = (sw[w] == scur) ? xin : 0.f;
-              p = fmaf(wv[w][v], xin, p);
-            }
-            p = fmaf(wv[W - 1][v], xc[v], p);
-            if constexpr (SEQ) p = (scur >= 0) ? p : 0.f;
-            gv *= silu_grad(p);
-          }
-          if constexpr (SEQ) gv = (scur >= 0) ? gv : 0.f;
-          g[v] = gv;
-        }
-        if (l < l1) {
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) {
-            db[v] += g[v];
-#pragma unroll
-            for (int w = 0; w < W - 1; ++w) {
-              float xin = xw[w][v];
-              if constexpr (SEQ) xin = (sw[w] == scur) ? xin : 0.f;
-              dw[w][v] = fmaf(g[v], xin, dw[w][v]);
-            }
-            dw[W - 1][v] = fmaf(g[v], xc[v], dw[W - 1][v]);
-          }
-        }
-        const int64_t e = l - (W - 1);
-        if (e >= emit_lo) {
-          float dxv[VEC];
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) {
-            float s = 0.f;
-#pragma unroll
-            for (int k = 0; k < W - 1; ++k) {
-              float gk = gw[k][v];
-              if constexpr (SEQ) gk = (sw[0] == sw[k]) ? gk : 0.f;
-              s = fmaf(wv[W - 1 - k][v], gk, s);
-            }
-            {
-              float gk = g[v];
-              if constexpr (SEQ) gk = (sw[0] == scur) ? gk : 0.f;
-              s = fmaf(wv[0][v], gk, s);
-            }
-            if (a.dfinal.data && e >= tail0)
-              s += load_any(a.dfinal.data, a.dfinal.dtype,
-                            b * a.dfinal.s0 + (d0 + v) * a.dfinal.s1 + (e - tail0) * a.dfinal.s2);
-            dxv[v] = s;
-          }
-          if (e >= 0) {
-            st_packet<T, VEC>(dxrow + e * a.dx.s2, pack<T, VEC>(dxv));
-          } else {
-#pragma unroll
-            for (int v = 0; v < VEC; ++v)
-              store_any(a.dinit.data, a.dinit.dtype,
-                        b * a.dinit.s0 + (d0 + v) * a.dinit.s1 + (e + W - 1) * a.dinit.s2, dxv[v]);
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < W - 2; ++k)
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) gw[k][v] = gw[k + 1][v];
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) gw[W - 2][v] = g[v];
-      }
-#pragma unroll
-      for (int k = 0; k < W - 2; ++k) {
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) xw[k][v] = xw[k + 1][v];
-        sw[k] = sw[k + 1];
-      }
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) xw[W - 2][v] = xc[v];
-      sw[W - 2] = scur;
+      checked_row(j, j % P);
     }
   }
   cp_async_wait<0>();
   __syncthreads();  // the rings are reused as the reduction buffer
 
-  // ---- deterministic dweight / dbias reduction (as in bwd_channel_last_kernel)
+  // ---- deterministic dweight / dbias reduction (fixed order over the CTA's segments)
   float* mine = red + (size_t)threadIdx.x * VEC * (W + 1);
 #pragma unroll
-  for (int v = 0; v < VEC; ++v) {
+  for (int i = 0; i < H; ++i) {
 #pragma unroll
-    for (int w = 0; w < W; ++w) mine[v * (W + 1) + w] = dw[w][v];
-    mine[v * (W + 1) + W] = db[v];
+    for (int w = 0; w < W; ++w) {
+      mine[(2 * i) * (W + 1) + w] = st.dw[w][i].x;
+      mine[(2 * i + 1) * (W + 1) + w] = st.dw[w][i].y;
+    }
+    mine[(2 * i) * (W + 1) + W] = st.db[i].x;
+    mine[(2 * i + 1) * (W + 1) + W] = st.db[i].y;
   }
   __syncthreads();
   const int ncol = TX * VEC * (W + 1);
   const int64_t dbeg = bx * TX * VEC;
   const int64_t slot = b * a.nby + by;
   float* dst = a.partials + slot * a.dim * (W + 1) + dbeg * (W + 1);
-  for (int o = threadIdx.x; o < ncol; o += kThreads) {
+  for (int o = threadIdx.x; o < ncol; o += NT) {
     float sum = 0.f;
     for (int r = 0; r < TY; ++r) sum += red[r * ncol + o];
     if (dbeg + o / (W + 1) < a.dim) dst[o] = sum;
   }
   if (arrive_last(a.counters + bx, (unsigned)(a.nby * a.batch))) {
-    reduce_tile_partials<W>(a, a.nby * a.batch, dbeg, TX * VEC);
+    reduce_tile_partials<W, NT>(a, a.nby * a.batch, dbeg, TX * VEC);
     if (threadIdx.x == 0) a.counters[bx] = 0;
   }
 }
@@ -719,7 +815,7 @@ static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 8) {
-#define CC1D_GO(SI, SQ) bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth><<<ls.grid, kThreads, ls.smem, s>>>(a)
+#define CC1D_GO(SI, SQ) bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kStreamThreads><<<ls.grid, kStreamThreads, ls.smem, s>>>(a)
       if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
       else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
 #undef CC1D_GO
@@ -766,7 +862,7 @@ template <typename T>
 static const void* bwd_kernel_ptr_t(const LaunchShape& ls) {
   constexpr int PV = 16 / sizeof(T);
   if (ls.layout == kLayoutStream)
-    return reinterpret_cast<const void*>(bwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepth>);
+    return reinterpret_cast<const void*>(bwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepth, kStreamThreads>);
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(bwd_channel_last_kernel<T, 4, PV, true, false, 2>);
     return reinterpret_cast<const void*>(bwd_channel_last_kernel<T, 4, 1, true, false, 2>);

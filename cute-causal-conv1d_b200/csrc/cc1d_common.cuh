@@ -132,34 +132,105 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // ------------------------------------------------------------------------ SiLU
-// Forward SiLU.  16-bit outputs use the single-MUFU identity
-// silu(p) = h * tanh(h) + h with h = p / 2 (sigmoid(p) = (1 + tanh(p/2)) / 2), whose
-// approximation error sits far below one 16-bit ulp.  fp32 outputs use
-// p / (1 + exp(-p)) with the fast exponential and a fast divide.
+// Hardware approximations (PTX): 2^v and 1/v, flushing subnormals to zero.
+__device__ __forceinline__ float ex2_approx(float v) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float v) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
 __device__ __forceinline__ float tanh_approx(float v) {
   float r;
   asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
   return r;
 }
 
+// exp(-p) = 2^(-p * log2(e)), clamped to 1e30 so that 1 + e and e * sigmoid stay finite
+// for very negative p (sigmoid(p) is then 1e-30, i.e. 0 to working precision).
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float exp_neg(float p) { return fminf(ex2_approx(-kLog2e * p), 1e30f); }
+
+// Forward SiLU.  16-bit outputs use the single-MUFU identity
+// silu(p) = h * tanh(h) + h with h = p / 2 (sigmoid(p) = (1 + tanh(p/2)) / 2); its
+// approximation error is far below the tolerance of a 16-bit result.  fp32 outputs use
+// p * sigmoid(p) with sigmoid(p) = 1 / (1 + exp(-p)).
 template <typename T>
 __device__ __forceinline__ float silu_fwd(float p) {
   if constexpr (std::is_same<T, float>::value) {
-    float e = fminf(__expf(-p), 1e30f);
-    return __fdividef(p, 1.0f + e);
+    return p * rcp_approx(1.0f + exp_neg(p));
   } else {
     float h = 0.5f * p;
     return fmaf(h, tanh_approx(h), h);
   }
 }
 
-// d silu(p) / dp = s * (1 + p * (1 - s)) with s = sigmoid(p).  Written with
-// e = exp(-p) so that 1 - s = e * s has no cancellation for large p; e is clamped
-// so that e * s stays finite for very negative p.
+// d silu(p) / dp = s * (1 + p * (1 - s)) with s = sigmoid(p); 1 - s = e * s with
+// e = exp(-p), which has no cancellation for large p.
 __device__ __forceinline__ float silu_grad(float p) {
-  float e = fminf(__expf(-p), 1e30f);
-  float s = __fdividef(1.0f, 1.0f + e);
+  const float e = exp_neg(p);
+  const float s = rcp_approx(1.0f + e);
   return s * fmaf(p, e * s, 1.0f);
+}
+
+// ------------------------------------------------------------ fp32x2 arithmetic
+// sm_100 executes fp32 FMA / MUL / ADD on register pairs in one instruction.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
+// Packet <-> fp32 pairs.
+template <typename T, int VEC>
+__device__ __forceinline__ void unpack2(const Packet<T, VEC>& r, float2 (&f)[VEC / 2]) {
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) {
+    if constexpr (std::is_same<T, float>::value)
+      f[i] = make_float2(r.v[2 * i], r.v[2 * i + 1]);
+    else if constexpr (std::is_same<T, __half>::value)
+      f[i] = __half22float2(*reinterpret_cast<const __half2*>(&r.v[2 * i]));
+    else
+      f[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.v[2 * i]));
+  }
+}
+template <typename T, int VEC>
+__device__ __forceinline__ Packet<T, VEC> pack2(const float2 (&f)[VEC / 2]) {
+  Packet<T, VEC> r;
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) {
+    if constexpr (std::is_same<T, float>::value) {
+      r.v[2 * i] = f[i].x;
+      r.v[2 * i + 1] = f[i].y;
+    } else if constexpr (std::is_same<T, __half>::value) {
+      *reinterpret_cast<__half2*>(&r.v[2 * i]) = __floats2half2_rn(f[i].x, f[i].y);
+    } else {
+      *reinterpret_cast<__nv_bfloat162*>(&r.v[2 * i]) = __floats2bfloat162_rn(f[i].x, f[i].y);
+    }
+  }
+  return r;
+}
+
+// SiLU of a pair whose argument was pre-scaled by 1/2 (h = p/2), 16-bit outputs:
+// silu(p) = h * tanh(h) + h.
+__device__ __forceinline__ float2 silu_half_arg2(float2 h) {
+  return ffma2(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h);
+}
+__device__ __forceinline__ float2 exp_neg2(float2 p) {
+  const float2 v = fmul2(make_float2(-kLog2e, -kLog2e), p);
+  return make_float2(fminf(ex2_approx(v.x), 1e30f), fminf(ex2_approx(v.y), 1e30f));
+}
+__device__ __forceinline__ float2 silu_exact2(float2 p) {
+  const float2 d = fadd2(make_float2(1.0f, 1.0f), exp_neg2(p));
+  return fmul2(p, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+}
+// d silu / dp of a pair (see silu_grad).
+__device__ __forceinline__ float2 silu_grad2(float2 p) {
+  const float2 e = exp_neg2(p);
+  const float2 d = fadd2(make_float2(1.0f, 1.0f), e);
+  const float2 s = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  return fmul2(s, ffma2(p, fmul2(e, s), make_float2(1.0f, 1.0f)));
 }
 
 // ------------------------------------------------------------- argument blocks

@@ -123,19 +123,24 @@ __global__ void __launch_bounds__(kThreads) fwd_channel_last_kernel(const ConvAr
 
 // ----------------------------------------------------- channel-last, streamed
 // One wave of persistent threads.  Thread (packet cv, segment) owns VEC channels and
-// the contiguous positions [l0, l1) of one batch row.  Rows stream through a private
-// ring of P shared-memory slots filled with cp.async (zero-filled outside [0, L)), so
-// P-1 rows per thread are in flight without occupying registers; the W-1 rows before
-// l0 enter the same stream first and only fill the register window.
-template <typename T, int W, int VEC, bool SILU, bool SEQ, int P>
-__global__ void __launch_bounds__(kThreads) fwd_stream_kernel(const ConvArgs a) {
+// the contiguous positions [l0, l1) of one batch row.  The W-1 rows before l0 (or the
+// initial states) are read once into the register window; rows l0 .. l1-1 then stream
+// through a private ring of P shared-memory slots filled with cp.async, so P-1 rows per
+// thread are in flight without occupying registers.  The row loop is unrolled by P
+// (compile-time ring slots, window rotation by register renaming) and has no bounds
+// checks; arithmetic runs on fp32 pairs (FFMA2).  With 16-bit SiLU the weights and
+// bias are pre-scaled by 1/2 so the accumulator is h = p/2 and silu(p) = h*tanh(h) + h.
+template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT>
+__global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   using Pk = Packet<T, VEC>;
+  constexpr int H = VEC / 2;
+  constexpr bool HALF_ARG = SILU && !std::is_same<T, float>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  Pk* ring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;  // slot s at ring[s * kThreads]
+  Pk* ring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;  // slot s at ring[s * NT]
   const int TX = 1 << a.tx_shift;
   const int tx = threadIdx.x & (TX - 1);
   const int ty = threadIdx.x >> a.tx_shift;
-  const int TY = kThreads >> a.tx_shift;
+  const int TY = NT >> a.tx_shift;
   const int64_t L = a.seqlen;
   int64_t t = blockIdx.x;
   const int64_t bx = t % a.nbx;
@@ -145,87 +150,113 @@ __global__ void __launch_bounds__(kThreads) fwd_stream_kernel(const ConvArgs a) 
   const int64_t cv = bx * TX + tx;
   const int64_t l0 = (by * TY + ty) * a.chunk;
   if (cv >= a.nv || l0 >= L) return;
-  const int64_t l1 = min(l0 + a.chunk, L);
+  const int n = static_cast<int>(min(l0 + a.chunk, L) - l0);
   const int64_t d0 = cv * VEC;
+  const int64_t sx = a.x.s2, so = a.out.s2;
+  const T* xsrc = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l0 * sx;
 
-  float wv[W][VEC], bv[VEC];
-  load_params<W, VEC>(a, d0, wv, bv);
-  const T* xrow = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0;
-  T* orow = static_cast<T*>(a.out.data) + b * a.out.s0 + d0;
-  const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
-
-  const int64_t lbeg = l0 - (W - 1);  // stream position j <-> row lbeg + j
-  const int n = static_cast<int>(l1 - lbeg);
-  auto issue = [&](int j) {
-    const int64_t l = lbeg + j;
-    const bool ok = l >= 0 && l < L;
-    cp_async_packet<sizeof(Pk)>(ring + (j % P) * kThreads, xrow + (ok ? l : 0) * a.x.s2, ok);
-  };
+  // prefetch rows l0 .. l0+P-2 before anything else
 #pragma unroll
   for (int j = 0; j < P - 1; ++j) {
-    if (j < n) issue(j);
+    if (j < n) cp_async_packet<sizeof(Pk)>(ring + j * NT, xsrc + j * sx, true);
     cp_async_commit();
   }
+  xsrc += (P - 1) * sx;
 
-  float xw[W - 1][VEC];
+  float2 wv[W][H], bv[H];
+  {
+    float wf[W][VEC], bf[VEC];
+    load_params<W, VEC>(a, d0, wf, bf);
+    const float sc = HALF_ARG ? 0.5f : 1.0f;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      bv[i] = make_float2(sc * bf[2 * i], sc * bf[2 * i + 1]);
+#pragma unroll
+      for (int w = 0; w < W; ++w) wv[w][i] = make_float2(sc * wf[w][2 * i], sc * wf[w][2 * i + 1]);
+    }
+  }
+  const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
+
+  // window: rows l0-(W-1) .. l0-1 (initial states, or zeros, before position 0)
+  float2 xw[W - 1][H];
   int sw[W - 1];
 #pragma unroll
   for (int k = 0; k < W - 1; ++k) {
+    const int64_t l = l0 - (W - 1) + k;
+    if (l >= 0) {
+      unpack2<T, VEC>(ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l * sx), xw[k]);
+    } else if (a.init.data) {
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) xw[k][v] = 0.f;
-    sw[k] = -1;
-  }
-  for (int j = 0; j < n; ++j) {
-    if (j + P - 1 < n) issue(j + P - 1);
-    cp_async_commit();
-    cp_async_wait<P - 1>();
-    const Pk raw = ring[(j % P) * kThreads];
-    const int64_t l = lbeg + j;
-    float xc[VEC];
-    unpack<T, VEC>(raw, xc);
-    if (l < 0 && a.init.data) {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v)
-        xc[v] = load_any(a.init.data, a.init.dtype, b * a.init.s0 + (d0 + v) * a.init.s1 + (W - 1 + l) * a.init.s2);
-    }
-    const int scur = (SEQ && l >= 0) ? srow[l * a.seq_idx.s1] : -1;
-    if (j >= W - 1) {
-      float acc[VEC];
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        float s = bv[v];
-#pragma unroll
-        for (int w = 0; w < W - 1; ++w) {
-          float xin = xw[w][v];
-          if constexpr (SEQ) xin = (sw[w] == scur) ? xin : 0.f;
-          s = fmaf(wv[w][v], xin, s);
-        }
-        s = fmaf(wv[W - 1][v], xc[v], s);
-        if constexpr (SEQ) s = (scur >= 0) ? s : 0.f;
-        if constexpr (SILU) s = silu_fwd<T>(s);
-        acc[v] = s;
+      for (int i = 0; i < H; ++i) {
+        const int64_t o = b * a.init.s0 + (d0 + 2 * i) * a.init.s1 + (W - 1 + l) * a.init.s2;
+        xw[k][i] = make_float2(load_any(a.init.data, a.init.dtype, o),
+                               load_any(a.init.data, a.init.dtype, o + a.init.s1));
       }
-      st_packet<T, VEC>(orow + l * a.out.s2, pack<T, VEC>(acc));
+    } else {
+#pragma unroll
+      for (int i = 0; i < H; ++i) xw[k][i] = make_float2(0.f, 0.f);
     }
+    sw[k] = (SEQ && l >= 0) ? srow[l * a.seq_idx.s1] : -1;
+  }
+
+  T* optr = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 + l0 * so;
+  const int* sptr = SEQ ? srow + l0 * a.seq_idx.s1 : nullptr;
+  for (int j0 = 0; j0 < n; j0 += P) {
 #pragma unroll
-    for (int k = 0; k < W - 2; ++k) {
+    for (int u = 0; u < P; ++u) {
+      const int j = j0 + u;
+      if (j < n) {
+        if (j + P - 1 < n) cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, true);
+        xsrc += sx;
+        cp_async_commit();
+        cp_async_wait<P - 1>();
+        float2 xc[H];
+        unpack2<T, VEC>(ring[u * NT], xc);
+        int scur = 0;
+        if constexpr (SEQ) {
+          scur = *sptr;
+          sptr += a.seq_idx.s1;
+        }
+        float2 acc[H];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) xw[k][v] = xw[k + 1][v];
-      sw[k] = sw[k + 1];
+        for (int i = 0; i < H; ++i) {
+          float2 s = bv[i];
+#pragma unroll
+          for (int w = 0; w < W - 1; ++w) {
+            float2 xin = xw[w][i];
+            if constexpr (SEQ) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
+            s = ffma2(wv[w][i], xin, s);
+          }
+          s = ffma2(wv[W - 1][i], xc[i], s);
+          if constexpr (SEQ) s = (scur >= 0) ? s : make_float2(0.f, 0.f);
+          if constexpr (SILU) s = HALF_ARG ? silu_half_arg2(s) : silu_exact2(s);
+          acc[i] = s;
+        }
+        st_packet<T, VEC>(optr, pack2<T, VEC>(acc));
+        optr += so;
+#pragma unroll
+        for (int k = 0; k < W - 2; ++k) {
+#pragma unroll
+          for (int i = 0; i < H; ++i) xw[k][i] = xw[k + 1][i];
+          sw[k] = sw[k + 1];
+        }
+#pragma unroll
+        for (int i = 0; i < H; ++i) xw[W - 2][i] = xc[i];
+        sw[W - 2] = scur;
+      }
     }
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) xw[W - 2][v] = xc[v];
-    sw[W - 2] = scur;
   }
   cp_async_wait<0>();
 
-  if (a.final_states.data && l1 == L) {
+  if (a.final_states.data && l0 + n == L) {
 #pragma unroll
     for (int k = 0; k < W - 1; ++k)
 #pragma unroll
-      for (int v = 0; v < VEC; ++v)
-        store_any(a.final_states.data, a.final_states.dtype,
-                  b * a.final_states.s0 + (d0 + v) * a.final_states.s1 + k * a.final_states.s2, xw[k][v]);
+      for (int i = 0; i < H; ++i) {
+        const int64_t o = b * a.final_states.s0 + (d0 + 2 * i) * a.final_states.s1 + k * a.final_states.s2;
+        store_any(a.final_states.data, a.final_states.dtype, o, xw[k][i].x);
+        store_any(a.final_states.data, a.final_states.dtype, o + a.final_states.s1, xw[k][i].y);
+      }
   }
 }
 
@@ -379,7 +410,7 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 16) {
-#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth><<<ls.grid, kThreads, ls.smem, s>>>(a)
+#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kStreamThreads><<<ls.grid, kStreamThreads, ls.smem, s>>>(a)
       if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
       else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
 #undef CC1D_GO
@@ -419,7 +450,7 @@ static const void* fwd_kernel_ptr_t(const LaunchShape& ls) {
   // host uses this only for occupancy queries.
   constexpr int PV = 16 / sizeof(T);
   if (ls.layout == kLayoutStream)
-    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, PV, true, false, kStreamDepth>);
+    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, PV, true, false, kStreamDepth, kStreamThreads>);
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, PV, true, false, 4>);
     return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, 1, true, false, 4>);
