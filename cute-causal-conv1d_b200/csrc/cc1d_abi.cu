@@ -47,23 +47,27 @@ int log2i(int v) {
   return s;
 }
 
-// 16-byte packets along dim (channel-last) are legal for this tensor.
-bool packet_ok_channel_last(const cc1d_tensor& t, int64_t dim) {
+// Stride s of a dimension of extent n keeps vec-element packets aligned (an extent-1
+// dimension never moves the pointer, whatever its stride).
+bool stride_ok(int64_t s, int64_t n, int vec) { return n <= 1 || s % vec == 0; }
+
+// 16-byte packets along dim (channel-last) are legal for this (B, D, L) tensor.
+bool packet_ok_channel_last(const cc1d_tensor& t, int64_t B, int64_t dim, int64_t L) {
   const int vec = 16 / elem_size(t.dtype);
-  return t.stride[1] == 1 && dim % vec == 0 && aligned16(t.data) && t.stride[0] % vec == 0 &&
-         t.stride[2] % vec == 0;
+  return t.stride[1] == 1 && dim % vec == 0 && aligned16(t.data) && stride_ok(t.stride[0], B, vec) &&
+         stride_ok(t.stride[2], L, vec);
 }
-// 16-byte packets along seqlen (rows) are legal for this tensor.
-bool packet_ok_rows(const cc1d_tensor& t) {
+// 16-byte packets along seqlen (rows) are legal for this (B, D, L) tensor.
+bool packet_ok_rows(const cc1d_tensor& t, int64_t B, int64_t D) {
   const int vec = 16 / elem_size(t.dtype);
-  return t.stride[2] == 1 && aligned16(t.data) && t.stride[0] % vec == 0 && t.stride[1] % vec == 0;
+  return t.stride[2] == 1 && aligned16(t.data) && stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[1], D, vec);
 }
 
-// Packets of `bytes` along dim (channel-last) are legal for this tensor.
-bool stream_ok(const cc1d_tensor& t, int64_t dim, int bytes) {
+// Packets of `bytes` along dim (channel-last) are legal for this (B, D, L) tensor.
+bool stream_ok(const cc1d_tensor& t, int64_t B, int64_t dim, int64_t L, int bytes) {
   const int vec = bytes / elem_size(t.dtype);
   return t.stride[1] == 1 && dim % vec == 0 && (reinterpret_cast<uintptr_t>(t.data) % bytes) == 0 &&
-         t.stride[0] % vec == 0 && t.stride[2] % vec == 0;
+         stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[2], L, vec);
 }
 
 int sm_count() {
@@ -180,7 +184,7 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   g.ls.width = width;
   g.ls.layout = kLayoutStream;
   g.ls.packet = true;
-  const int vec = (bwd ? 8 : 16) / es;
+  const int vec = 8 / es;  // both streamed kernels move 8-byte packets
   const int64_t nv = D / vec;
   const int TX = (int)std::min<int64_t>(32, pow2_ceil(nv));
   const int TY = kStreamThreads / TX;
@@ -198,7 +202,7 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   g.ntiles = nbx * nby * B;
   g.nslots = nby * B;
   g.ncounters = nbx;
-  g.ls.smem = (size_t)kStreamDepth * kStreamThreads * 16;
+  g.ls.smem = bwd ? (size_t)kStreamDepth * kStreamThreads * 16 : (size_t)kStreamDepthFwd * kStreamThreads * 8;
   return g;
 }
 
@@ -269,18 +273,18 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
   bool packet = false;
   const int es = elem_size(p->x.dtype);
   Geometry g;
-  if (stream_ok(p->x, D, 16) && stream_ok(p->out, D, 16)) {
+  if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->out, B, D, L, 8)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
-    const size_t smem = (size_t)kStreamDepth * kStreamThreads * 16;
+    const size_t smem = (size_t)kStreamDepthFwd * kStreamThreads * 8;
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), smem, kStreamThreads) * sm_count();
     g = plan_stream(false, B, D, L, W, es, resident);
   } else {
     if (p->x.stride[1] == 1 && p->out.stride[1] == 1) {
-      packet = packet_ok_channel_last(p->x, D) && packet_ok_channel_last(p->out, D);
+      packet = packet_ok_channel_last(p->x, B, D, L) && packet_ok_channel_last(p->out, B, D, L);
     } else if (p->x.stride[2] == 1 && p->out.stride[2] == 1) {
       layout = kLayoutRows;
-      packet = packet_ok_rows(p->x) && packet_ok_rows(p->out);
+      packet = packet_ok_rows(p->x, B, D) && packet_ok_rows(p->out, B, D);
     }
     g = plan(false, B, D, L, W, layout, packet, es);
   }
@@ -330,7 +334,7 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
   int layout = kLayoutChannelLast;
   bool packet = false;
   const int es = elem_size(p->x.dtype);
-  if (stream_ok(p->x, D, 8) && stream_ok(p->dout, D, 8) && stream_ok(p->dx, D, 8)) {
+  if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->dout, B, D, L, 8) && stream_ok(p->dx, B, D, L, 8)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
     const size_t smem = (size_t)kStreamDepth * kStreamThreads * 16;
@@ -339,11 +343,11 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
     return CC1D_OK;
   }
   if (p->x.stride[1] == 1 && p->dout.stride[1] == 1 && p->dx.stride[1] == 1) {
-    packet = packet_ok_channel_last(p->x, D) && packet_ok_channel_last(p->dout, D) &&
-             packet_ok_channel_last(p->dx, D);
+    packet = packet_ok_channel_last(p->x, B, D, L) && packet_ok_channel_last(p->dout, B, D, L) &&
+             packet_ok_channel_last(p->dx, B, D, L);
   } else if (p->x.stride[2] == 1 && p->dout.stride[2] == 1 && p->dx.stride[2] == 1) {
     layout = kLayoutRows;
-    packet = packet_ok_rows(p->x) && packet_ok_rows(p->dout) && packet_ok_rows(p->dx);
+    packet = packet_ok_rows(p->x, B, D) && packet_ok_rows(p->dout, B, D) && packet_ok_rows(p->dx, B, D);
   }
   *out_g = plan(true, B, D, L, (int)p->width, layout, packet, es);
   return CC1D_OK;
@@ -438,10 +442,10 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   if (!p->x.data || !p->conv_state.data || !p->weight.data || !p->out.data)
     return fail(CC1D_ERR_VALUE, "x, conv_state, weight and out are required");
   const int vec = 16 / elem_size(p->x.dtype);
-  auto ok = [&](const cc1d_tensor& t) {
-    return t.stride[1] == 1 && aligned16(t.data) && t.stride[0] % vec == 0 && t.stride[2] % vec == 0;
+  auto ok = [&](const cc1d_tensor& t, int64_t n0, int64_t n2) {
+    return t.stride[1] == 1 && aligned16(t.data) && stride_ok(t.stride[0], n0, vec) && stride_ok(t.stride[2], n2, vec);
   };
-  const bool packet = D % vec == 0 && ok(p->x) && ok(p->out) && ok(p->conv_state);
+  const bool packet = D % vec == 0 && ok(p->x, B, T) && ok(p->out, B, T) && ok(p->conv_state, p->state_batch, S);
   UpdateArgs a;
   std::memset(&a, 0, sizeof(a));
   a.batch = B;
@@ -483,8 +487,8 @@ cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* p, void* 
     return fail(CC1D_ERR_VALUE, "x, cu_seqlens and states are required");
   const int vec = 16 / elem_size(p->x.dtype);
   const bool packet = D % vec == 0 && p->x.stride[1] == 1 && p->states.stride[1] == 1 && aligned16(p->x.data) &&
-                      aligned16(p->states.data) && p->x.stride[0] % vec == 0 && p->states.stride[0] % vec == 0 &&
-                      p->states.stride[2] % vec == 0;
+                      aligned16(p->states.data) && stride_ok(p->x.stride[0], p->total_tokens, vec) &&
+                      stride_ok(p->states.stride[0], B, vec) && stride_ok(p->states.stride[2], S, vec);
   VarlenArgs a;
   std::memset(&a, 0, sizeof(a));
   a.batch = B;

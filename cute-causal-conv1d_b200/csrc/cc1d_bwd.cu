@@ -347,11 +347,11 @@ struct BwdWalk {
 
 // One wave of persistent threads; thread (packet cv, segment) owns VEC channels and
 // positions [l0, l1) of one batch row.  The x rows l0-(W-1) .. l0-1 (or initial states)
-// are read once into the window; x and dout rows l0 .. min(l1+W-1, L)-1 stream through
-// private cp.async rings.  Row l produces g[l] (and dweight/dbias terms when l < l1) and
-// dx[l-(W-1)].  The first W-1 rows (which may emit dinitial_states) and the W-1 rows
-// past l1 (dfinal_states, rows past L) run a checked path; the rows in between run an
-// unrolled loop with compile-time ring slots and no checks.
+// are read once into the window; x and dout rows l0 .. l1+W-2 stream through private
+// cp.async rings (zero filled past L, so g vanishes there without a check).  Row l
+// produces g[l] (dweight/dbias terms when l < l1) and dx[l-(W-1)]; the loop runs in
+// unrolled blocks of P rows with compile-time ring slots and predicated prefetch, and
+// only the rare rows (dinitial_states, dfinal_states) branch.
 template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT>
 __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
   using Pk = Packet<T, VEC>;
@@ -391,16 +391,13 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
     const int64_t sx = a.x.s2, sg = a.dout.s2, sd = a.dx.s2;
     const T* xsrc = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l0 * sx;
     const T* gsrc = static_cast<const T*>(a.dout.data) + b * a.dout.s0 + d0 + l0 * sg;
-    // stream row j <-> position l0 + j; ring slot j % P
-    auto issue = [&](int j, int slot) {
-      if (j < nload) {
-        cp_async_packet<sizeof(Pk)>(xring + slot * NT, xsrc + j * sx, true);
-        cp_async_packet<sizeof(Pk)>(gring + slot * NT, gsrc + j * sg, true);
-      }
-    };
+    // stream row j <-> position l0 + j, ring slot j % P; rows past the data are zero filled
 #pragma unroll
     for (int j = 0; j < P - 1; ++j) {
-      issue(j, j);
+      cp_async_packet<sizeof(Pk)>(xring + j * NT, xsrc, j < nload);
+      cp_async_packet<sizeof(Pk)>(gring + j * NT, gsrc, j < nload);
+      xsrc += sx;
+      gsrc += sg;
       cp_async_commit();
     }
 
@@ -435,27 +432,26 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
       for (int i = 0; i < H; ++i) st.gw[k][i] = make_float2(0.f, 0.f);
       st.sw[k] = (SEQ && l >= 0) ? srow[l * a.seq_idx.s1] : -1;
     }
-    T* dxbase = static_cast<T*>(a.dx.data) + b * a.dx.s0 + d0;
     const int64_t tail0 = L - (W - 1);
-    const bool want_dinit = l0 == 0 && a.dinit.data != nullptr;
+    // row j emits dx at e = l0 + j - (W-1): rows j >= W-1 of every segment, plus the first
+    // W-1 rows of the first segment when dinitial_states are wanted (e < 0)
+    const int emit0 = (l0 == 0 && a.dinit.data != nullptr) ? 0 : W - 1;
+    T* dxptr = static_cast<T*>(a.dx.data) + b * a.dx.s0 + d0 + (l0 - (W - 1)) * sd;
+    const int* sptr = SEQ ? srow + l0 * a.seq_idx.s1 : nullptr;
 
-    // checked row: dx of position e = l-(W-1) goes to dx (e >= l0), to dinitial
-    // (e < 0, first segment), or nowhere; dfinal_states is added on the tail.
-    auto checked_row = [&](int j, int slot) {
-      const int64_t l = l0 + j;
+    auto row = [&](int j, const Pk& rx, const Pk& rg) {
       float2 xc[H], gc[H];
-      if (j < nload) {
-        unpack2<T, VEC>(xring[slot * NT], xc);
-        unpack2<T, VEC>(gring[slot * NT], gc);
-      } else {
-#pragma unroll
-        for (int i = 0; i < H; ++i) xc[i] = gc[i] = make_float2(0.f, 0.f);
+      unpack2<T, VEC>(rx, xc);
+      unpack2<T, VEC>(rg, gc);
+      int scur = 0;
+      if constexpr (SEQ) {
+        scur = j < nload ? *sptr : -1;
+        sptr += a.seq_idx.s1;
       }
-      const int scur = (SEQ && j < nload) ? srow[l * a.seq_idx.s1] : -1;
-      const int64_t e = l - (W - 1);
       float2 dxv[H];
       st.template step<true, true>(xc, gc, scur, j < nmain, dxv);
-      if (e >= l0 || (e < 0 && want_dinit)) {
+      if (j >= emit0) {
+        const int64_t e = l0 + j - (W - 1);
         if (a.dfinal.data && e >= tail0) {
 #pragma unroll
           for (int i = 0; i < H; ++i) {
@@ -465,7 +461,7 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
           }
         }
         if (e >= 0) {
-          st_packet<T, VEC>(dxbase + e * sd, pack2<T, VEC>(dxv));
+          st_packet<T, VEC>(dxptr, pack2<T, VEC>(dxv));
         } else {
 #pragma unroll
           for (int i = 0; i < H; ++i) {
@@ -475,51 +471,32 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
           }
         }
       }
+      dxptr += sd;
     };
-
-    // head: rows 0 .. W-2
-#pragma unroll
-    for (int j = 0; j < W - 1; ++j) {
-      if (j < nall) {
-        issue(j + P - 1, (j + P - 1) % P);
-        cp_async_commit();
-        cp_async_wait<P - 1>();
-        checked_row(j, j % P);
-      }
-    }
-    // steady state: rows W-1 .. nmain-1 (full data, accumulate, dx at e >= l0)
-    const int jsteady_end = nmain;
-    const int* sptr = SEQ ? srow + (l0 + W - 1) * a.seq_idx.s1 : nullptr;
-    T* dxptr = dxbase + l0 * sd;
-    for (int j0 = W - 1; j0 < jsteady_end; j0 += P) {
+    // full blocks of P rows: compile-time ring slots, predicated prefetch
+    int j0 = 0;
+    for (; j0 + P <= nall; j0 += P) {
 #pragma unroll
       for (int u = 0; u < P; ++u) {
-        const int j = j0 + u;
-        if (j < jsteady_end) {
-          issue(j + P - 1, (u + W - 1 + P - 1) % P);
-          cp_async_commit();
-          cp_async_wait<P - 1>();
-          float2 xc[H], gc[H];
-          unpack2<T, VEC>(xring[((u + W - 1) % P) * NT], xc);
-          unpack2<T, VEC>(gring[((u + W - 1) % P) * NT], gc);
-          int scur = 0;
-          if constexpr (SEQ) {
-            scur = *sptr;
-            sptr += a.seq_idx.s1;
-          }
-          float2 dxv[H];
-          st.template step<true, true>(xc, gc, scur, true, dxv);
-          st_packet<T, VEC>(dxptr, pack2<T, VEC>(dxv));
-          dxptr += sd;
-        }
+        const bool ok = j0 + u + P - 1 < nload;
+        cp_async_packet<sizeof(Pk)>(xring + ((u + P - 1) % P) * NT, xsrc, ok);
+        cp_async_packet<sizeof(Pk)>(gring + ((u + P - 1) % P) * NT, gsrc, ok);
+        xsrc += sx;
+        gsrc += sg;
+        cp_async_commit();
+        cp_async_wait<P - 1>();
+        row(j0 + u, xring[u * NT], gring[u * NT]);
       }
     }
-    // tail: rows max(W-1, nmain) .. nall-1
-    for (int j = max(W - 1, nmain); j < nall; ++j) {
-      issue(j + P - 1, (j + P - 1) % P);
+    for (int j = j0; j < nall; ++j) {  // remainder
+      const bool ok = j + P - 1 < nload;
+      cp_async_packet<sizeof(Pk)>(xring + ((j + P - 1) % P) * NT, xsrc, ok);
+      cp_async_packet<sizeof(Pk)>(gring + ((j + P - 1) % P) * NT, gsrc, ok);
+      xsrc += sx;
+      gsrc += sg;
       cp_async_commit();
       cp_async_wait<P - 1>();
-      checked_row(j, j % P);
+      row(j, xring[(j % P) * NT], gring[(j % P) * NT]);
     }
   }
   cp_async_wait<0>();

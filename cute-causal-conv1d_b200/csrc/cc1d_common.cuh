@@ -46,8 +46,8 @@ __device__ __forceinline__ void store_any(void* p, int dt, int64_t i, float v) {
 }
 
 // ------------------------------------------------------------ VEC-element packets
-// A packet is VEC consecutive elements; for VEC*sizeof(T) == 16 it moves as one
-// 128-bit access, otherwise element by element.
+// A packet is VEC consecutive elements; 4-, 8- and 16-byte packets move as one
+// access (the caller guarantees the alignment), others element by element.
 template <typename T, int VEC> struct alignas(sizeof(T) * VEC) Packet { T v[VEC]; };
 
 template <typename T, int VEC>
@@ -55,6 +55,12 @@ __device__ __forceinline__ Packet<T, VEC> ld_packet(const T* p) {
   Packet<T, VEC> r;
   if constexpr (sizeof(T) * VEC == 16) {
     uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    r = *reinterpret_cast<Packet<T, VEC>*>(&u);
+  } else if constexpr (sizeof(T) * VEC == 8) {
+    uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    r = *reinterpret_cast<Packet<T, VEC>*>(&u);
+  } else if constexpr (sizeof(T) * VEC == 4) {
+    unsigned u = __ldg(reinterpret_cast<const unsigned*>(p));
     r = *reinterpret_cast<Packet<T, VEC>*>(&u);
   } else {
 #pragma unroll
@@ -67,6 +73,10 @@ template <typename T, int VEC>
 __device__ __forceinline__ void st_packet(T* p, const Packet<T, VEC>& r) {
   if constexpr (sizeof(T) * VEC == 16) {
     *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(&r);
+  } else if constexpr (sizeof(T) * VEC == 8) {
+    *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(&r);
+  } else if constexpr (sizeof(T) * VEC == 4) {
+    *reinterpret_cast<unsigned*>(p) = *reinterpret_cast<const unsigned*>(&r);
   } else {
 #pragma unroll
     for (int i = 0; i < VEC; ++i) p[i] = r.v[i];
@@ -182,17 +192,20 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return _
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 
-// Packet <-> fp32 pairs.
+// Packet <-> fp32 pairs.  A bf16 is the upper half of an fp32, so a bf16 pair widens
+// with one shift and one mask.
 template <typename T, int VEC>
 __device__ __forceinline__ void unpack2(const Packet<T, VEC>& r, float2 (&f)[VEC / 2]) {
 #pragma unroll
   for (int i = 0; i < VEC / 2; ++i) {
-    if constexpr (std::is_same<T, float>::value)
+    if constexpr (std::is_same<T, float>::value) {
       f[i] = make_float2(r.v[2 * i], r.v[2 * i + 1]);
-    else if constexpr (std::is_same<T, __half>::value)
+    } else if constexpr (std::is_same<T, __half>::value) {
       f[i] = __half22float2(*reinterpret_cast<const __half2*>(&r.v[2 * i]));
-    else
-      f[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.v[2 * i]));
+    } else {
+      const unsigned u = *reinterpret_cast<const unsigned*>(&r.v[2 * i]);
+      f[i] = make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+    }
   }
 }
 template <typename T, int VEC>

@@ -155,13 +155,13 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   const int64_t sx = a.x.s2, so = a.out.s2;
   const T* xsrc = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l0 * sx;
 
-  // prefetch rows l0 .. l0+P-2 before anything else
+  // prefetch rows l0 .. l0+P-2 before anything else (rows past the segment: zero fill)
 #pragma unroll
   for (int j = 0; j < P - 1; ++j) {
-    if (j < n) cp_async_packet<sizeof(Pk)>(ring + j * NT, xsrc + j * sx, true);
+    cp_async_packet<sizeof(Pk)>(ring + j * NT, xsrc, j < n);
+    xsrc += sx;
     cp_async_commit();
   }
-  xsrc += (P - 1) * sx;
 
   float2 wv[W][H], bv[H];
   {
@@ -201,50 +201,59 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
 
   T* optr = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 + l0 * so;
   const int* sptr = SEQ ? srow + l0 * a.seq_idx.s1 : nullptr;
-  for (int j0 = 0; j0 < n; j0 += P) {
+  auto row = [&](const Pk& raw) {
+    float2 xc[H];
+    unpack2<T, VEC>(raw, xc);
+    int scur = 0;
+    if constexpr (SEQ) {
+      scur = *sptr;
+      sptr += a.seq_idx.s1;
+    }
+    float2 acc[H];
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      float2 s = bv[i];
+#pragma unroll
+      for (int w = 0; w < W - 1; ++w) {
+        float2 xin = xw[w][i];
+        if constexpr (SEQ) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
+        s = ffma2(wv[w][i], xin, s);
+      }
+      s = ffma2(wv[W - 1][i], xc[i], s);
+      if constexpr (SEQ) s = (scur >= 0) ? s : make_float2(0.f, 0.f);
+      if constexpr (SILU) s = HALF_ARG ? silu_half_arg2(s) : silu_exact2(s);
+      acc[i] = s;
+    }
+    st_packet<T, VEC>(optr, pack2<T, VEC>(acc));
+    optr += so;
+#pragma unroll
+    for (int k = 0; k < W - 2; ++k) {
+#pragma unroll
+      for (int i = 0; i < H; ++i) xw[k][i] = xw[k + 1][i];
+      sw[k] = sw[k + 1];
+    }
+#pragma unroll
+    for (int i = 0; i < H; ++i) xw[W - 2][i] = xc[i];
+    sw[W - 2] = scur;
+  };
+  // full blocks of P rows: compile-time ring slots, predicated prefetch, no branches
+  int j0 = 0;
+  for (; j0 + P <= n; j0 += P) {
 #pragma unroll
     for (int u = 0; u < P; ++u) {
-      const int j = j0 + u;
-      if (j < n) {
-        if (j + P - 1 < n) cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, true);
-        xsrc += sx;
-        cp_async_commit();
-        cp_async_wait<P - 1>();
-        float2 xc[H];
-        unpack2<T, VEC>(ring[u * NT], xc);
-        int scur = 0;
-        if constexpr (SEQ) {
-          scur = *sptr;
-          sptr += a.seq_idx.s1;
-        }
-        float2 acc[H];
-#pragma unroll
-        for (int i = 0; i < H; ++i) {
-          float2 s = bv[i];
-#pragma unroll
-          for (int w = 0; w < W - 1; ++w) {
-            float2 xin = xw[w][i];
-            if constexpr (SEQ) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
-            s = ffma2(wv[w][i], xin, s);
-          }
-          s = ffma2(wv[W - 1][i], xc[i], s);
-          if constexpr (SEQ) s = (scur >= 0) ? s : make_float2(0.f, 0.f);
-          if constexpr (SILU) s = HALF_ARG ? silu_half_arg2(s) : silu_exact2(s);
-          acc[i] = s;
-        }
-        st_packet<T, VEC>(optr, pack2<T, VEC>(acc));
-        optr += so;
-#pragma unroll
-        for (int k = 0; k < W - 2; ++k) {
-#pragma unroll
-          for (int i = 0; i < H; ++i) xw[k][i] = xw[k + 1][i];
-          sw[k] = sw[k + 1];
-        }
-#pragma unroll
-        for (int i = 0; i < H; ++i) xw[W - 2][i] = xc[i];
-        sw[W - 2] = scur;
-      }
+      cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
+      xsrc += sx;
+      cp_async_commit();
+      cp_async_wait<P - 1>();
+      row(ring[u * NT]);
     }
+  }
+  for (int j = j0; j < n; ++j) {  // remainder
+    cp_async_packet<sizeof(Pk)>(ring + ((j + P - 1) % P) * NT, xsrc, j + P - 1 < n);
+    xsrc += sx;
+    cp_async_commit();
+    cp_async_wait<P - 1>();
+    row(ring[(j % P) * NT]);
   }
   cp_async_wait<0>();
 
@@ -409,8 +418,8 @@ template <typename T, int W, int VEC>
 static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
-    if constexpr (VEC * sizeof(T) == 16) {
-#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kStreamThreads><<<ls.grid, kStreamThreads, ls.smem, s>>>(a)
+    if constexpr (VEC * sizeof(T) == 8) {
+#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kStreamThreads><<<ls.grid, kStreamThreads, ls.smem, s>>>(a)
       if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
       else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
 #undef CC1D_GO
@@ -433,6 +442,15 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
 template <typename T>
 static cudaError_t launch_fwd_t(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   constexpr int PV = 16 / sizeof(T);
+  constexpr int SV = 8 / sizeof(T);  // the streamed kernel moves 8-byte packets
+  if (ls.layout == kLayoutStream) {
+    switch (ls.width) {
+      case 2: return launch_fwd_w<T, 2, SV>(a, ls, s);
+      case 3: return launch_fwd_w<T, 3, SV>(a, ls, s);
+      case 4: return launch_fwd_w<T, 4, SV>(a, ls, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (ls.width * 2 + (ls.packet ? 1 : 0)) {
     case 4: return launch_fwd_w<T, 2, 1>(a, ls, s);
     case 5: return launch_fwd_w<T, 2, PV>(a, ls, s);
@@ -450,7 +468,7 @@ static const void* fwd_kernel_ptr_t(const LaunchShape& ls) {
   // host uses this only for occupancy queries.
   constexpr int PV = 16 / sizeof(T);
   if (ls.layout == kLayoutStream)
-    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, PV, true, false, kStreamDepth, kStreamThreads>);
+    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepthFwd, kStreamThreads>);
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, PV, true, false, 4>);
     return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, 1, true, false, 4>);

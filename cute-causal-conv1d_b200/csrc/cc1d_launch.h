@@ -13,7 +13,8 @@ namespace cc1d {
 constexpr int kLayoutChannelLast = 0;  // stride over dim == 1
 constexpr int kLayoutRows = 1;         // stride over seqlen == 1
 constexpr int kLayoutStream = 2;       // channel-last, per-thread cp.async row stream
-constexpr int kStreamDepth = 8;        // rows in flight per thread (ring slots)
+constexpr int kStreamDepth = 8;        // backward: rows in flight per thread (ring slots)
+constexpr int kStreamDepthFwd = 8;     // forward: rows in flight per thread
 constexpr int kStreamThreads = 128;    // CTA size of the streamed kernels
 
 struct LaunchShape {
