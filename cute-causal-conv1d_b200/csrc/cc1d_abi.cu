@@ -441,9 +441,10 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   if (B == 0 || D == 0 || T == 0) return CC1D_OK;
   if (!p->x.data || !p->conv_state.data || !p->weight.data || !p->out.data)
     return fail(CC1D_ERR_VALUE, "x, conv_state, weight and out are required");
-  const int vec = 16 / elem_size(p->x.dtype);
+  const int vec = 8 / elem_size(p->x.dtype);  // 8-byte packets along dim
   auto ok = [&](const cc1d_tensor& t, int64_t n0, int64_t n2) {
-    return t.stride[1] == 1 && aligned16(t.data) && stride_ok(t.stride[0], n0, vec) && stride_ok(t.stride[2], n2, vec);
+    return t.stride[1] == 1 && (reinterpret_cast<uintptr_t>(t.data) % 8) == 0 && stride_ok(t.stride[0], n0, vec) &&
+           stride_ok(t.stride[2], n2, vec);
   };
   const bool packet = D % vec == 0 && ok(p->x, B, T) && ok(p->out, B, T) && ok(p->conv_state, p->state_batch, S);
   UpdateArgs a;
@@ -462,7 +463,7 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   a.indices = static_cast<const int32_t*>(p->conv_state_indices.data);
   a.indices_stride = p->conv_state_indices.stride[0];
   a.silu = p->silu;
-  a.weight_vec = packet && p->weight.dtype == CC1D_FLOAT32 && p->weight.stride[1] == 1 &&
+  a.weight_vec = packet && (vec * W) % 4 == 0 && p->weight.dtype == CC1D_FLOAT32 && p->weight.stride[1] == 1 &&
                  p->weight.stride[0] == W && aligned16(p->weight.data);
   const int64_t nv = (D + (packet ? vec : 1) - 1) / (packet ? vec : 1);
   const int64_t blocks = ((nv + 31) / 32) * ((B + 7) / 8);

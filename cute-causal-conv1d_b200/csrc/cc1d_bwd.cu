@@ -349,9 +349,10 @@ struct BwdWalk {
 // positions [l0, l1) of one batch row.  The x rows l0-(W-1) .. l0-1 (or initial states)
 // are read once into the window; x and dout rows l0 .. l1+W-2 stream through private
 // cp.async rings (zero filled past L, so g vanishes there without a check).  Row l
-// produces g[l] (dweight/dbias terms when l < l1) and dx[l-(W-1)]; the loop runs in
-// unrolled blocks of P rows with compile-time ring slots and predicated prefetch, and
-// only the rare rows (dinitial_states, dfinal_states) branch.
+// produces g[l] (dweight/dbias terms when l < l1) and dx[l-(W-1)].  The first W-1 rows
+// (dinitial_states) and the W-1 rows past l1 (dfinal_states) take a checked path; the
+// rows between run unrolled blocks of P rows with compile-time ring slots, predicated
+// prefetch and no branches.
 template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT>
 __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
   using Pk = Packet<T, VEC>;
@@ -437,17 +438,15 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
     // W-1 rows of the first segment when dinitial_states are wanted (e < 0)
     const int emit0 = (l0 == 0 && a.dinit.data != nullptr) ? 0 : W - 1;
     T* dxptr = static_cast<T*>(a.dx.data) + b * a.dx.s0 + d0 + (l0 - (W - 1)) * sd;
-    const int* sptr = SEQ ? srow + l0 * a.seq_idx.s1 : nullptr;
 
-    auto row = [&](int j, const Pk& rx, const Pk& rg) {
+    // Rows with a rare case: accumulation stops at nmain, dx of position
+    // e = l0 + j - (W-1) goes to dinitial_states (e < 0) or gets dfinal_states (e >= L-(W-1)).
+    auto generic_row = [&](int j, const Pk& rx, const Pk& rg) {
       float2 xc[H], gc[H];
       unpack2<T, VEC>(rx, xc);
       unpack2<T, VEC>(rg, gc);
       int scur = 0;
-      if constexpr (SEQ) {
-        scur = j < nload ? *sptr : -1;
-        sptr += a.seq_idx.s1;
-      }
+      if constexpr (SEQ) scur = j < nload ? srow[(l0 + j) * a.seq_idx.s1] : -1;
       float2 dxv[H];
       st.template step<true, true>(xc, gc, scur, j < nmain, dxv);
       if (j >= emit0) {
@@ -473,30 +472,56 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
       }
       dxptr += sd;
     };
-    // full blocks of P rows: compile-time ring slots, predicated prefetch
-    int j0 = 0;
-    for (; j0 + P <= nall; j0 += P) {
-#pragma unroll
-      for (int u = 0; u < P; ++u) {
-        const bool ok = j0 + u + P - 1 < nload;
-        cp_async_packet<sizeof(Pk)>(xring + ((u + P - 1) % P) * NT, xsrc, ok);
-        cp_async_packet<sizeof(Pk)>(gring + ((u + P - 1) % P) * NT, gsrc, ok);
-        xsrc += sx;
-        gsrc += sg;
-        cp_async_commit();
-        cp_async_wait<P - 1>();
-        row(j0 + u, xring[u * NT], gring[u * NT]);
+    // Steady rows (W-1 <= j < nmain): accumulate, emit dx at e >= l0, nothing rare.
+    const int* sptr = SEQ ? srow + (l0 + W - 1) * a.seq_idx.s1 : nullptr;
+    auto steady_row = [&](const Pk& rx, const Pk& rg) {
+      float2 xc[H], gc[H];
+      unpack2<T, VEC>(rx, xc);
+      unpack2<T, VEC>(rg, gc);
+      int scur = 0;
+      if constexpr (SEQ) {
+        scur = *sptr;
+        sptr += a.seq_idx.s1;
       }
-    }
-    for (int j = j0; j < nall; ++j) {  // remainder
+      float2 dxv[H];
+      st.template step<true, true>(xc, gc, scur, true, dxv);
+      st_packet<T, VEC>(dxptr, pack2<T, VEC>(dxv));
+      dxptr += sd;
+    };
+    auto prefetch = [&](int j, int slot) {  // row j + P - 1 into `slot`
       const bool ok = j + P - 1 < nload;
-      cp_async_packet<sizeof(Pk)>(xring + ((j + P - 1) % P) * NT, xsrc, ok);
-      cp_async_packet<sizeof(Pk)>(gring + ((j + P - 1) % P) * NT, gsrc, ok);
+      cp_async_packet<sizeof(Pk)>(xring + slot * NT, xsrc, ok);
+      cp_async_packet<sizeof(Pk)>(gring + slot * NT, gsrc, ok);
       xsrc += sx;
       gsrc += sg;
       cp_async_commit();
       cp_async_wait<P - 1>();
-      row(j, xring[(j % P) * NT], gring[(j % P) * NT]);
+    };
+    // head: rows 0 .. W-2
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      if (j < nall) {
+        prefetch(j, (j + P - 1) % P);
+        generic_row(j, xring[j * NT], gring[j * NT]);
+      }
+    }
+    // steady: rows W-1 .. nmain-1 in unrolled blocks of P (compile-time slots), then the rest
+    int j = W - 1;
+    for (; j + P <= nmain; j += P) {
+#pragma unroll
+      for (int u = 0; u < P; ++u) {
+        prefetch(j + u, (u + W - 1 + P - 1) % P);
+        steady_row(xring[((u + W - 1) % P) * NT], gring[((u + W - 1) % P) * NT]);
+      }
+    }
+    for (; j < nmain; ++j) {
+      prefetch(j, (j + P - 1) % P);
+      steady_row(xring[(j % P) * NT], gring[(j % P) * NT]);
+    }
+    // tail: rows max(W-1, nmain) .. nall-1 (no accumulation; dfinal_states; zeros past L)
+    for (j = max(W - 1, nmain); j < nall; ++j) {
+      prefetch(j, (j + P - 1) % P);
+      generic_row(j, xring[(j % P) * NT], gring[(j % P) * NT]);
     }
   }
   cp_async_wait<0>();

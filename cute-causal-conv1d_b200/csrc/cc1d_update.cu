@@ -3,8 +3,8 @@
 // update: one thread per (batch row, VEC channels).  The output window is
 // [state history | x]; outputs read the old state; the state is written after every
 // output of the row is computed, by the same thread, so the in-place shift needs no
-// synchronisation.  With channel-last x and state the VEC channels move as one 16-byte
-// packet (512 contiguous bytes per warp); other layouts use VEC = 1 with the same code.
+// synchronisation.  With channel-last x and state the VEC channels move as one 8-byte
+// packet (256 contiguous bytes per warp); other layouts use VEC = 1 with the same code.
 //
 // varlen states: one thread per (sequence, state slot, VEC channels), a pure gather
 // of the last state_len tokens of each packed sequence (zero where the sequence is
@@ -108,11 +108,20 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
       for (int64_t t = 0; t < T_len; ++t)  // in order: with seqlen > state_len the last write wins
         st_packet<T, VEC>(sp + pos_mod(cache + t, S) * a.state.s2, ld_packet<T, VEC>(xp + t * a.x.s2));
     } else {
-      for (int64_t s = 0; s < S; ++s) {  // ascending: each source is read before it is overwritten
-        const int64_t src = s + T_len;
-        Packet<T, VEC> v = (src < S) ? ld_packet<T, VEC>(sp + src * a.state.s2)
-                                     : ld_packet<T, VEC>(xp + (src - S) * a.x.s2);
-        st_packet<T, VEC>(sp + s * a.state.s2, v);
+      // new[s] = old[s + T] (s + T < S) or x[s + T - S].  Positions move down, so a group
+      // of G positions is read completely before it is written, in ascending groups.
+      constexpr int G = 4;
+      for (int64_t s0 = 0; s0 < S; s0 += G) {
+        Packet<T, VEC> v[G];
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+          const int64_t src = s0 + q + T_len;
+          if (s0 + q < S)
+            v[q] = (src < S) ? ld_packet<T, VEC>(sp + src * a.state.s2) : ld_packet<T, VEC>(xp + (src - S) * a.x.s2);
+        }
+#pragma unroll
+        for (int q = 0; q < G; ++q)
+          if (s0 + q < S) st_packet<T, VEC>(sp + (s0 + q) * a.state.s2, v[q]);
       }
     }
   }
@@ -147,7 +156,7 @@ __global__ void __launch_bounds__(kThreads) varlen_states_kernel(const VarlenArg
 
 template <typename T>
 static cudaError_t launch_update_t(const UpdateArgs& a, int width, bool packet, dim3 grid, cudaStream_t s) {
-  constexpr int PV = 16 / sizeof(T);
+  constexpr int PV = 8 / sizeof(T);  // 8-byte packets: more threads, fewer registers per thread
   switch (width * 2 + (packet ? 1 : 0)) {
     case 4: update_kernel<T, 2, 1><<<grid, kThreads, 0, s>>>(a); break;
     case 5: update_kernel<T, 2, PV><<<grid, kThreads, 0, s>>>(a); break;
