@@ -362,7 +362,7 @@ def run_ours(args):
                      "algorithmic_bytes": bb},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 3 * args.steps,  # forward kernel + backward kernel + partial-sum kernel
         "clocks": sampler.result(),
         "kernels": kernels,
     }

@@ -70,6 +70,12 @@ bool stream_ok(const cc1d_tensor& t, int64_t B, int64_t dim, int64_t L, int byte
          stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[2], L, vec);
 }
 
+// (batch, dim, seqlen)-contiguous rows whose starts are 16-byte aligned.
+bool rows_stream_ok(const cc1d_tensor& t, int64_t B, int64_t D) {
+  const int vec = 16 / elem_size(t.dtype);
+  return t.stride[2] == 1 && aligned16(t.data) && stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[1], D, vec);
+}
+
 int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -102,6 +108,13 @@ int blocks_per_sm(const void* kernel, size_t smem, int threads = kThreads) {
 }
 
 const void* kernel_ptr(bool bwd, int dtype, const LaunchShape& ls) {
+  if (ls.layout == kLayoutRowStream) {
+    switch (dtype) {
+      case CC1D_FLOAT32: return rows_kernel_ptr_f32(bwd);
+      case CC1D_FLOAT16: return rows_kernel_ptr_f16(bwd);
+      default: return rows_kernel_ptr_bf16(bwd);
+    }
+  }
   switch (dtype) {
     case CC1D_FLOAT32: return bwd ? bwd_kernel_ptr_f32(ls) : fwd_kernel_ptr_f32(ls);
     case CC1D_FLOAT16: return bwd ? bwd_kernel_ptr_f16(ls) : fwd_kernel_ptr_f16(ls);
@@ -110,6 +123,13 @@ const void* kernel_ptr(bool bwd, int dtype, const LaunchShape& ls) {
 }
 
 cudaError_t dispatch(bool bwd, int dtype, const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
+  if (ls.layout == kLayoutRowStream) {
+    switch (dtype) {
+      case CC1D_FLOAT32: return rows_f32(bwd, a, ls, s);
+      case CC1D_FLOAT16: return rows_f16(bwd, a, ls, s);
+      default: return rows_bf16(bwd, a, ls, s);
+    }
+  }
   switch (dtype) {
     case CC1D_FLOAT32: return bwd ? bwd_f32(a, ls, s) : fwd_f32(a, ls, s);
     case CC1D_FLOAT16: return bwd ? bwd_f16(a, ls, s) : fwd_f16(a, ls, s);
@@ -121,10 +141,11 @@ cudaError_t dispatch(bool bwd, int dtype, const ConvArgs& a, const LaunchShape& 
 // the problem (not on the device) except for the final grid size.
 struct Geometry {
   LaunchShape ls;
-  ConvArgs a;        // geometry fields only
+  ConvArgs a;             // geometry fields only
   int64_t ntiles;
-  int64_t nslots;    // backward partial slots per channel tile
-  int64_t ncounters; // backward channel tiles
+  int64_t nslots;         // backward partial slots per channel tile
+  int64_t ncounters;      // backward channel tiles (arrival counters)
+  int64_t partial_floats; // backward workspace floats for partial sums
 };
 
 Geometry plan(bool bwd, int64_t B, int64_t D, int64_t L, int width, int layout, bool packet, int es) {
@@ -151,6 +172,7 @@ Geometry plan(bool bwd, int64_t B, int64_t D, int64_t L, int width, int layout, 
     g.ntiles = g.a.nbx * g.a.nby * B;
     g.nslots = g.a.nby * B;
     g.ncounters = g.a.nbx;
+    g.partial_floats = g.nslots * D * (width + 1);
     g.ls.smem = bwd ? (size_t)kThreads * vec * (width + 1) * sizeof(float) : 0;
   } else {
     const int gmin = vec == 1 ? 4 : 1;  // a round must span at least W-1 positions
@@ -170,14 +192,41 @@ Geometry plan(bool bwd, int64_t B, int64_t D, int64_t L, int width, int layout, 
     g.ntiles = g.a.nbx * nck * B;
     g.nslots = nck * B;
     g.ncounters = g.a.nbx;
+    g.partial_floats = g.nslots * D * (width + 1);
     g.ls.smem = 0;
   }
   return g;
 }
 
-// Streamed channel-last kernels: one wave of CTAs, each thread a contiguous row segment.
-// The segment count per channel column is chosen so the grid fits the resident CTA
-// capacity (no second, partial wave).
+// Number of warp units for `ncol` columns of `len` steps each (at most max_seg segments
+// per column) on `target` resident warps.  Estimated time ~ waves x (longest segment +
+// per-unit start-up cost, in steps); among one-wave and multi-wave splits pick the
+// smallest estimate (ties: fewer units).
+int64_t choose_units(int64_t ncol, int64_t len, int64_t max_seg, int64_t target, int64_t unit_overhead) {
+  auto cost = [&](int64_t u) {
+    const int64_t q = u / ncol;  // every column has at least q segments
+    return ((u + target - 1) / target) * ((len + q - 1) / q + unit_overhead);
+  };
+  int64_t units = std::min<int64_t>(std::max<int64_t>(target, ncol), ncol * max_seg);
+  int64_t best = cost(units);
+  for (int64_t k = 1; k <= 4; ++k) {
+    const int64_t cands[2] = {k * target, ((k * target) / ncol) * ncol};
+    for (int64_t u : cands) {
+      if (u < ncol || u > ncol * max_seg) continue;
+      const int64_t c = cost(u);
+      if (c < best || (c == best && u < units)) {
+        best = c;
+        units = u;
+      }
+    }
+  }
+  return units;
+}
+
+// Streamed channel-last kernels: one wave of warps.  A warp column (32 packets of one
+// batch row) is cut into seg_q or seg_q+1 sequence segments so that the number of warp
+// units equals the resident warp capacity and every warp gets the same number of rows
+// (+-1 row, +-1 segment length between columns).
 Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_blocks) {
   Geometry g;
   std::memset(&g, 0, sizeof(g));
@@ -186,30 +235,54 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   g.ls.packet = true;
   const int vec = 8 / es;  // both streamed kernels move 8-byte packets
   const int64_t nv = D / vec;
-  const int TX = (int)std::min<int64_t>(32, pow2_ceil(nv));
-  const int TY = kStreamThreads / TX;
-  const int64_t min_rows = bwd ? 64 : 32;
-  const int64_t nbx = (nv + TX - 1) / TX;
-  int64_t nby = std::max<int64_t>(1, resident_blocks / std::max<int64_t>(1, nbx * B));
-  int64_t seg = (L + nby * TY - 1) / (nby * TY);
-  if (seg < min_rows) seg = min_rows;
-  nby = ((L + seg - 1) / seg + TY - 1) / TY;
-  g.a.tx_shift = log2i(TX);
+  const int64_t warps_per_block = kStreamThreads / 32;
+  const int64_t ncol = B * ((nv + 31) / 32);
+  const int64_t min_rows = bwd ? 32 : 16;
+  const int64_t max_seg = std::max<int64_t>(1, L / min_rows);
+  const int64_t target = std::max<int64_t>(1, resident_blocks * warps_per_block);
+  const int64_t units = choose_units(ncol, L, max_seg, target, /*unit_overhead=*/24);
   g.a.nv = nv;
-  g.a.chunk = seg;
-  g.a.nbx = nbx;
-  g.a.nby = nby;
-  g.ntiles = nbx * nby * B;
-  g.nslots = nby * B;
-  g.ncounters = nbx;
+  g.a.ncol = ncol;
+  g.a.seg_q = units / ncol;
+  g.a.seg_r = units % ncol;
+  g.a.units = units;
+  g.ntiles = (units + warps_per_block - 1) / warps_per_block;
+  g.ncounters = 0;  // partials are summed by a second kernel
+  g.partial_floats = units * 32 * vec * (width + 1);
   g.ls.smem = bwd ? (size_t)kStreamDepth * kStreamThreads * 16 : (size_t)kStreamDepthFwd * kStreamThreads * 8;
+  return g;
+}
+
+// Row-stream kernels ((B, D, L) contiguous): lane = channel, warp = 32 channels of one
+// batch row and a segment of 32-byte steps along the sequence.
+Geometry plan_rows(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_blocks) {
+  Geometry g;
+  std::memset(&g, 0, sizeof(g));
+  g.ls.width = width;
+  g.ls.layout = kLayoutRowStream;
+  g.ls.packet = true;
+  const int64_t C = 32 / es;
+  const int64_t ncol = B * ((D + 31) / 32);
+  const int64_t nsteps = (L + C - 1) / C;
+  const int64_t max_seg = std::max<int64_t>(1, nsteps / (bwd ? 4 : 2));
+  const int64_t target = std::max<int64_t>(1, resident_blocks * (kStreamThreads / 32));
+  const int64_t units = choose_units(ncol, nsteps, max_seg, target, /*unit_overhead=*/4);
+  g.a.nv = D;  // one channel per lane
+  g.a.ncol = ncol;
+  g.a.seg_q = units / ncol;
+  g.a.seg_r = units % ncol;
+  g.a.units = units;
+  g.ntiles = (units + kStreamThreads / 32 - 1) / (kStreamThreads / 32);
+  g.ncounters = 0;  // partials are summed by a second kernel
+  g.partial_floats = units * 32 * (width + 1);
+  g.ls.smem = (size_t)2 * kRowDepthBwd * kStreamThreads * 32;
   return g;
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
-int64_t bwd_workspace_for(const Geometry& g, int64_t D, int width) {
-  const int64_t part = round_up(g.nslots * D * (width + 1) * (int64_t)sizeof(float), 256);
+int64_t bwd_workspace_for(const Geometry& g) {
+  const int64_t part = round_up(g.partial_floats * (int64_t)sizeof(float), 256);
   return part + round_up(g.ncounters * (int64_t)sizeof(unsigned int), 256);
 }
 
@@ -301,7 +374,7 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
   a.out = tensor_arg(p->out);
   g.ls.silu = p->silu != 0;
   g.ls.seq = p->seq_idx.data != nullptr;
-  if (g.ls.layout == kLayoutStream) {
+  if (g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream) {
     g.ls.grid = dim3((unsigned)g.ntiles);
   } else {
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, g.ls), g.ls.smem) * sm_count();
@@ -342,6 +415,15 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
     *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }
+  if (p->x.stride[1] != 1 && rows_stream_ok(p->x, B, D) && rows_stream_ok(p->dout, B, D) &&
+      rows_stream_ok(p->dx, B, D)) {
+    LaunchShape probe{};
+    probe.layout = kLayoutRowStream;
+    const size_t smem = (size_t)2 * kRowDepthBwd * kStreamThreads * 32;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kStreamThreads) * sm_count();
+    *out_g = plan_rows(true, B, D, L, (int)p->width, es, resident);
+    return CC1D_OK;
+  }
   if (p->x.stride[1] == 1 && p->dout.stride[1] == 1 && p->dx.stride[1] == 1) {
     packet = packet_ok_channel_last(p->x, B, D, L) && packet_ok_channel_last(p->dout, B, D, L) &&
              packet_ok_channel_last(p->dx, B, D, L);
@@ -359,7 +441,7 @@ int64_t cc1d_bwd_workspace_bytes(const cc1d_bwd_params* p) {
   bool empty = false;
   if (bwd_prepare(p, &g, &empty) != CC1D_OK) return -1;
   if (empty) return 0;
-  return bwd_workspace_for(g, p->dim, (int)p->width);
+  return bwd_workspace_for(g);
 }
 
 cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
@@ -382,7 +464,7 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
     }
     return e == cudaSuccess ? CC1D_OK : cuda_fail(e, "causal_conv1d backward zero fill");
   }
-  const int64_t need = bwd_workspace_for(g, D, W);
+  const int64_t need = bwd_workspace_for(g);
   if (!p->workspace || p->workspace_bytes < need)
     return fail(CC1D_ERR_VALUE, "workspace too small: %lld bytes needed", (long long)need);
   if (!aligned16(p->workspace)) return fail(CC1D_ERR_VALUE, "workspace must be 16-byte aligned");
@@ -403,12 +485,15 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
   a.dbias = p->bias.data ? p->dbias : nullptr;
   char* ws = static_cast<char*>(p->workspace);
   a.partials = reinterpret_cast<float*>(ws);
-  a.counters = reinterpret_cast<unsigned int*>(ws + round_up(g.nslots * D * (W + 1) * (int64_t)sizeof(float), 256));
+  a.counters = reinterpret_cast<unsigned int*>(ws + round_up(g.partial_floats * (int64_t)sizeof(float), 256));
   g.ls.silu = p->silu != 0;
   g.ls.seq = p->seq_idx.data != nullptr;
-  cudaError_t e = cudaMemsetAsync(a.counters, 0, g.ncounters * sizeof(unsigned int), s);
-  if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward counter reset");
-  if (g.ls.layout == kLayoutStream) {
+  cudaError_t e = cudaSuccess;
+  if (g.ncounters > 0) {
+    e = cudaMemsetAsync(a.counters, 0, g.ncounters * sizeof(unsigned int), s);
+    if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward counter reset");
+  }
+  if (g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream) {
     g.ls.grid = dim3((unsigned)g.ntiles);
   } else {
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, g.ls), g.ls.smem) * sm_count();
@@ -416,7 +501,8 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
   }
   e = dispatch(true, p->x.dtype, a, g.ls, s);
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward launch");
-  g_launches.fetch_add(1);
+  // the streamed layouts add a second kernel that sums the partials
+  g_launches.fetch_add(g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream ? 2 : 1);
   return CC1D_OK;
 }
 
@@ -466,7 +552,7 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   a.weight_vec = packet && (vec * W) % 4 == 0 && p->weight.dtype == CC1D_FLOAT32 && p->weight.stride[1] == 1 &&
                  p->weight.stride[0] == W && aligned16(p->weight.data);
   const int64_t nv = (D + (packet ? vec : 1) - 1) / (packet ? vec : 1);
-  const int64_t blocks = ((nv + 31) / 32) * ((B + 7) / 8);
+  const int64_t blocks = ((nv + 31) / 32) * ((B + 8 * kUpdateRows - 1) / (8 * kUpdateRows));
   cudaError_t e = launch_update(p->x.dtype, a, (int)W, packet, dim3((unsigned)std::max<int64_t>(1, blocks)),
                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d update launch");

@@ -345,8 +345,8 @@ struct BwdWalk {
   }
 };
 
-// One wave of persistent threads; thread (packet cv, segment) owns VEC channels and
-// positions [l0, l1) of one batch row.  The x rows l0-(W-1) .. l0-1 (or initial states)
+// One wave of persistent warps (see WarpUnit): lane = one VEC-channel packet, warp =
+// 32 consecutive packets of one batch row and one segment [l0, l1).  The x rows l0-(W-1) .. l0-1 (or initial states)
 // are read once into the window; x and dout rows l0 .. l1+W-2 stream through private
 // cp.async rings (zero filled past L, so g vanishes there without a check).  Row l
 // produces g[l] (dweight/dbias terms when l < l1) and dx[l-(W-1)].  The first W-1 rows
@@ -360,20 +360,17 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Pk* xring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
   Pk* gring = reinterpret_cast<Pk*>(smem_raw) + P * NT + threadIdx.x;
-  float* red = reinterpret_cast<float*>(smem_raw);  // reused after the stream drains
-  const int TX = 1 << a.tx_shift;
-  const int tx = threadIdx.x & (TX - 1);
-  const int ty = threadIdx.x >> a.tx_shift;
-  const int TY = NT >> a.tx_shift;
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
+  if (unit >= a.units) return;  // whole warps only
+  const WarpUnit wu = warp_unit(a, unit);
+  const int64_t pb = wu.col / a.batch;  // packet block
+  const int64_t b = wu.col - pb * a.batch;
+  const int64_t cv = pb * 32 + lane;
   const int64_t L = a.seqlen;
-  int64_t t = blockIdx.x;
-  const int64_t bx = t % a.nbx;
-  t /= a.nbx;
-  const int64_t by = t % a.nby;
-  const int64_t b = t / a.nby;
-  const int64_t cv = bx * TX + tx;
-  const int64_t l0 = (by * TY + ty) * a.chunk;
-  const bool active = cv < a.nv && l0 < L;
+  const int64_t l0 = wu.seg * L / wu.nseg;
+  const int64_t l1_seg = (wu.seg + 1) * L / wu.nseg;
+  const bool active = cv < a.nv && l0 < l1_seg;
   const int64_t d0 = cv * VEC;
 
   BwdWalk<T, W, VEC, SILU, SEQ> st;
@@ -385,7 +382,7 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
   }
 
   if (active) {
-    const int64_t l1 = min(l0 + a.chunk, L);
+    const int64_t l1 = l1_seg;
     const int nmain = static_cast<int>(l1 - l0);                   // rows that accumulate
     const int nload = static_cast<int>(min(l1 + (W - 1), L) - l0);  // rows with data
     const int nall = nmain + (W - 1);                                // rows walked
@@ -525,10 +522,11 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
     }
   }
   cp_async_wait<0>();
-  __syncthreads();  // the rings are reused as the reduction buffer
 
-  // ---- deterministic dweight / dbias reduction (fixed order over the CTA's segments)
-  float* mine = red + (size_t)threadIdx.x * VEC * (W + 1);
+  // ---- dweight / dbias: each warp unit writes its partial sums to its own slot; the
+  // next kernel (reduce_unit_partials) adds the slots of each channel in unit order.
+  constexpr int PER_LANE = VEC * (W + 1);
+  float* mine = a.partials + (unit * 32 + lane) * PER_LANE;
 #pragma unroll
   for (int i = 0; i < H; ++i) {
 #pragma unroll
@@ -539,20 +537,42 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
     mine[(2 * i) * (W + 1) + W] = st.db[i].x;
     mine[(2 * i + 1) * (W + 1) + W] = st.db[i].y;
   }
-  __syncthreads();
-  const int ncol = TX * VEC * (W + 1);
-  const int64_t dbeg = bx * TX * VEC;
-  const int64_t slot = b * a.nby + by;
-  float* dst = a.partials + slot * a.dim * (W + 1) + dbeg * (W + 1);
-  for (int o = threadIdx.x; o < ncol; o += NT) {
-    float sum = 0.f;
-    for (int r = 0; r < TY; ++r) sum += red[r * ncol + o];
-    if (dbeg + o / (W + 1) < a.dim) dst[o] = sum;
+}
+
+// Deterministic sum of the warp-unit partials of the streamed backward kernels.  Slot
+// layout [unit][32 lanes][PER_LANE]; lane l of packet block pb covers channels
+// (pb*32 + l)*VEC .. +VEC-1 and PER_LANE = VEC*(W+1) values (W weights, then bias, per
+// channel).  One thread per (packet block, lane, value); the units of packet block pb
+// (all batch rows, all segments) are contiguous and are added in order with four
+// independent chains combined in a fixed order.
+template <int W, int VEC>
+__global__ void __launch_bounds__(kThreads) reduce_unit_partials(const ConvArgs a) {
+  constexpr int PER_LANE = VEC * (W + 1);
+  const int64_t npb = (a.nv + 31) / 32;
+  const int64_t t = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  if (t >= npb * 32 * PER_LANE) return;
+  const int64_t pb = t / (32 * PER_LANE);
+  const int rem = static_cast<int>(t - pb * 32 * PER_LANE);
+  const int lane = rem / PER_LANE;
+  const int q = rem - lane * PER_LANE;
+  const int64_t d = (pb * 32 + lane) * VEC + q / (W + 1);
+  if (d >= a.dim) return;
+  const int w = q % (W + 1);
+  const int64_t u0 = first_unit(a, pb * a.batch), u1 = first_unit(a, (pb + 1) * a.batch);
+  const float* src = a.partials + rem;
+  const int64_t stride = 32 * PER_LANE;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  int64_t k = u0;
+  for (; k + 4 <= u1; k += 4) {
+    s0 += __ldcg(src + (k + 0) * stride);
+    s1 += __ldcg(src + (k + 1) * stride);
+    s2 += __ldcg(src + (k + 2) * stride);
+    s3 += __ldcg(src + (k + 3) * stride);
   }
-  if (arrive_last(a.counters + bx, (unsigned)(a.nby * a.batch))) {
-    reduce_tile_partials<W, NT>(a, a.nby * a.batch, dbeg, TX * VEC);
-    if (threadIdx.x == 0) a.counters[bx] = 0;
-  }
+  for (; k < u1; ++k) s0 += __ldcg(src + k * stride);
+  const float s = (s0 + s1) + (s2 + s3);
+  if (w < W) a.dweight[d * W + w] = s;
+  else if (a.dbias) a.dbias[d] = s;
 }
 
 // ------------------------------------------------------------------- rows
@@ -821,6 +841,10 @@ static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
       if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
       else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
 #undef CC1D_GO
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+      const int64_t n = ((a.nv + 31) / 32) * 32 * VEC * (W + 1);
+      reduce_unit_partials<W, VEC><<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, 0, s>>>(a);
     }
   } else if (ls.layout == kLayoutChannelLast) {
     constexpr int U = 2;
@@ -875,6 +899,19 @@ static const void* bwd_kernel_ptr_t(const LaunchShape& ls) {
 
 cudaError_t CC1D_DT_NAME(bwd)(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   return launch_bwd_t<CC1D_DT_TYPE>(a, ls, s);
+}
+
+// Sum of the row-stream kernel's warp-unit partials (one channel per lane: VEC = 1).
+cudaError_t CC1D_DT_NAME(reduce_rows)(const ConvArgs& a, int width, cudaStream_t s) {
+  const int64_t n = ((a.nv + 31) / 32) * 32 * (width + 1);
+  const unsigned grid = (unsigned)((n + kThreads - 1) / kThreads);
+  switch (width) {
+    case 2: reduce_unit_partials<2, 1><<<grid, kThreads, 0, s>>>(a); break;
+    case 3: reduce_unit_partials<3, 1><<<grid, kThreads, 0, s>>>(a); break;
+    case 4: reduce_unit_partials<4, 1><<<grid, kThreads, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
 }
 
 const void* CC1D_DT_NAME(bwd_kernel_ptr)(const LaunchShape& ls) {

@@ -279,7 +279,41 @@ struct ConvArgs {
   int g_shift;              // row kernels: log2 of lanes per row group
   int rounds;               // row kernels: rounds per chunk
   int64_t nck;              // row kernels: chunks per row
+  // streamed kernels: work is split into warp units.  A warp column is 32 consecutive
+  // channel packets (packet block pb) of one batch row b, numbered col = pb * batch + b;
+  // columns < seg_r are cut into seg_q + 1 sequence segments, the others into seg_q;
+  // unit u is one (column, segment).  The units of one packet block are contiguous.
+  int64_t ncol, seg_q, seg_r, units;
 };
+
+// First warp unit of column c (c == ncol gives the total).
+__host__ __device__ inline int64_t first_unit(const ConvArgs& a, int64_t c) {
+  return c < a.seg_r ? c * (a.seg_q + 1) : a.seg_r * (a.seg_q + 1) + (c - a.seg_r) * a.seg_q;
+}
+
+// The (column, segment) of warp unit u, the column's segment count and its first unit.
+struct WarpUnit {
+  int64_t col, seg, nseg, first;
+};
+__device__ __forceinline__ WarpUnit warp_unit(const ConvArgs& a, int64_t u) {
+  WarpUnit w;
+  const int64_t q1 = a.seg_q + 1;
+  const int64_t big = a.seg_r * q1;
+  if (u < big) {
+    w.col = u / q1;
+    w.seg = u - w.col * q1;
+    w.nseg = q1;
+    w.first = w.col * q1;
+  } else {
+    const int64_t v = u - big;
+    const int64_t c = v / a.seg_q;
+    w.col = a.seg_r + c;
+    w.seg = v - c * a.seg_q;
+    w.nseg = a.seg_q;
+    w.first = big + c * a.seg_q;
+  }
+  return w;
+}
 
 // Weight and bias of VEC consecutive channels, as fp32.
 template <int W, int VEC>

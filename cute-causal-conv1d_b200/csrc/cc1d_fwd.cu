@@ -122,8 +122,8 @@ __global__ void __launch_bounds__(kThreads) fwd_channel_last_kernel(const ConvAr
 }
 
 // ----------------------------------------------------- channel-last, streamed
-// One wave of persistent threads.  Thread (packet cv, segment) owns VEC channels and
-// the contiguous positions [l0, l1) of one batch row.  The W-1 rows before l0 (or the
+// One wave of persistent warps (see WarpUnit): lane = one VEC-channel packet, warp =
+// 32 consecutive packets of one batch row and one sequence segment [l0, l1).  The W-1 rows before l0 (or the
 // initial states) are read once into the register window; rows l0 .. l1-1 then stream
 // through a private ring of P shared-memory slots filled with cp.async, so P-1 rows per
 // thread are in flight without occupying registers.  The row loop is unrolled by P
@@ -137,20 +137,18 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   constexpr bool HALF_ARG = SILU && !std::is_same<T, float>::value;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Pk* ring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;  // slot s at ring[s * NT]
-  const int TX = 1 << a.tx_shift;
-  const int tx = threadIdx.x & (TX - 1);
-  const int ty = threadIdx.x >> a.tx_shift;
-  const int TY = NT >> a.tx_shift;
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
+  if (unit >= a.units) return;
+  const WarpUnit wu = warp_unit(a, unit);
+  const int64_t pb = wu.col / a.batch;  // packet block
+  const int64_t b = wu.col - pb * a.batch;
+  const int64_t cv = pb * 32 + lane;
   const int64_t L = a.seqlen;
-  int64_t t = blockIdx.x;
-  const int64_t bx = t % a.nbx;
-  t /= a.nbx;
-  const int64_t by = t % a.nby;
-  const int64_t b = t / a.nby;
-  const int64_t cv = bx * TX + tx;
-  const int64_t l0 = (by * TY + ty) * a.chunk;
-  if (cv >= a.nv || l0 >= L) return;
-  const int n = static_cast<int>(min(l0 + a.chunk, L) - l0);
+  const int64_t l0 = wu.seg * L / wu.nseg;
+  const int64_t l1 = (wu.seg + 1) * L / wu.nseg;
+  if (cv >= a.nv || l0 >= l1) return;
+  const int n = static_cast<int>(l1 - l0);
   const int64_t d0 = cv * VEC;
   const int64_t sx = a.x.s2, so = a.out.s2;
   const T* xsrc = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l0 * sx;

@@ -16,6 +16,8 @@ constexpr int kLayoutStream = 2;       // channel-last, per-thread cp.async row 
 constexpr int kStreamDepth = 8;        // backward: rows in flight per thread (ring slots)
 constexpr int kStreamDepthFwd = 8;     // forward: rows in flight per thread
 constexpr int kStreamThreads = 128;    // CTA size of the streamed kernels
+constexpr int kLayoutRowStream = 3;    // (batch, dim, seqlen)-contiguous, per-lane sector stream
+constexpr int kRowDepthBwd = 4;        // row-stream backward: ring slots (32-byte sectors) per lane and tensor
 
 struct LaunchShape {
   dim3 grid;
@@ -38,6 +40,16 @@ struct LaunchShape {
 CC1D_DECLARE(fwd)
 CC1D_DECLARE(bwd)
 #undef CC1D_DECLARE
+
+cudaError_t rows_f32(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
+cudaError_t rows_f16(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
+cudaError_t rows_bf16(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
+const void* rows_kernel_ptr_f32(bool bwd);
+const void* rows_kernel_ptr_f16(bool bwd);
+const void* rows_kernel_ptr_bf16(bool bwd);
+cudaError_t reduce_rows_f32(const ConvArgs&, int width, cudaStream_t);
+cudaError_t reduce_rows_f16(const ConvArgs&, int width, cudaStream_t);
+cudaError_t reduce_rows_bf16(const ConvArgs&, int width, cudaStream_t);
 
 }  // namespace cc1d
 

@@ -21,69 +21,93 @@ __device__ __forceinline__ int64_t pos_mod(int64_t v, int64_t m) {
 
 template <typename T, int W, int VEC>
 __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
-  // CTA tile: 32 channel packets x 8 batch rows, so the 8 warps of a CTA read the same
-  // weights (the second to eighth reads hit L1).
+  // CTA tile: 32 channel packets x (8 warps x BR batch rows).  A thread owns one packet
+  // for BR batch rows: it loads the weights once, issues the loads of all BR rows before
+  // using any of them (the rows' memory latencies overlap), then computes and writes.
+  constexpr int BR = kUpdateRows;
   const int tx = threadIdx.x & 31;
   const int ty = threadIdx.x >> 5;
   const int64_t nv = (a.dim + VEC - 1) / VEC;
   const int64_t nbx = (nv + 31) / 32;
   const int64_t cv = (blockIdx.x % nbx) * 32 + tx;
-  const int64_t b = (blockIdx.x / nbx) * 8 + ty;
-  if (cv < nv && b < a.batch) {
-    const int64_t d0 = cv * VEC;
-    const int64_t T_len = a.seqlen;
-    const int64_t S = a.state_len;
-    const T* xp = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1;
-    T* op = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 * a.out.s1;
+  const int64_t b0 = ((blockIdx.x / nbx) * 8 + ty) * BR;
+  if (cv >= nv || b0 >= a.batch) return;
+  const int64_t d0 = cv * VEC;
+  const int64_t T_len = a.seqlen;
+  const int64_t S = a.state_len;
 
-    float wv[W][VEC], bv[VEC];
-    if (a.weight_vec) {  // contiguous fp32 (dim, W): this thread's VEC*W weights are adjacent
-      const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.weight.data) + d0 * W);
-      float flat[VEC * W];
+  float wv[W][VEC], bv[VEC];
+  if (a.weight_vec) {  // contiguous fp32 (dim, W): this thread's VEC*W weights are adjacent
+    const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.weight.data) + d0 * W);
+    float flat[VEC * W];
 #pragma unroll
-      for (int q = 0; q < VEC * W / 4; ++q) {
-        const float4 f = __ldg(wp + q);
-        flat[4 * q] = f.x;
-        flat[4 * q + 1] = f.y;
-        flat[4 * q + 2] = f.z;
-        flat[4 * q + 3] = f.w;
-      }
-#pragma unroll
-      for (int v = 0; v < VEC; ++v)
-#pragma unroll
-        for (int w = 0; w < W; ++w) wv[w][v] = flat[v * W + w];
-    } else {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v)
-#pragma unroll
-        for (int w = 0; w < W; ++w)
-          wv[w][v] = load_any(a.weight.data, a.weight.dtype, (d0 + v) * a.weight.s0 + w * a.weight.s1);
+    for (int q = 0; q < VEC * W / 4; ++q) {
+      const float4 f = __ldg(wp + q);
+      flat[4 * q] = f.x;
+      flat[4 * q + 1] = f.y;
+      flat[4 * q + 2] = f.z;
+      flat[4 * q + 3] = f.w;
     }
 #pragma unroll
     for (int v = 0; v < VEC; ++v)
-      bv[v] = a.bias.data ? load_any(a.bias.data, a.bias.dtype, (d0 + v) * a.bias.s0) : 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) wv[w][v] = flat[v * W + w];
+  } else {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v)
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        wv[w][v] = load_any(a.weight.data, a.weight.dtype, (d0 + v) * a.weight.s0 + w * a.weight.s1);
+  }
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) bv[v] = a.bias.data ? load_any(a.bias.data, a.bias.dtype, (d0 + v) * a.bias.s0) : 0.f;
 
-    const int64_t row = a.indices ? (int64_t)a.indices[b * a.indices_stride] : b;
-    if (row < 0) {  // padded batch row: zero output, state untouched
+  // phase 1: row indices, then every row's history window and first input
+  int64_t row[BR], cache[BR];
+  bool ok[BR];
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    const int64_t b = b0 + r;
+    ok[r] = b < a.batch;
+    row[r] = (ok[r] && a.indices) ? (int64_t)a.indices[b * a.indices_stride] : b;
+    cache[r] = (ok[r] && a.cache_seqlens) ? (int64_t)a.cache_seqlens[b * a.cache_stride] : 0;
+  }
+  Packet<T, VEC> hist[BR][W - 1], x0[BR];
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    if (!ok[r]) continue;
+    const T* xp = static_cast<const T*>(a.x.data) + (b0 + r) * a.x.s0 + d0 * a.x.s1;
+    x0[r] = ld_packet<T, VEC>(xp);
+    if (row[r] >= 0) {
+      const T* sp = static_cast<const T*>(a.state.data) + row[r] * a.state.s0 + d0 * a.state.s1;
+#pragma unroll
+      for (int i = 0; i < W - 1; ++i) {
+        const int64_t pos = a.cache_seqlens ? pos_mod(cache[r] - (W - 1) + i, S) : S - (W - 1) + i;
+        hist[r][i] = ld_packet<T, VEC>(sp + pos * a.state.s2);
+      }
+    }
+  }
+
+  // phase 2: outputs (the window is [history | x]; outputs use the old state)
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    if (!ok[r]) continue;
+    const int64_t b = b0 + r;
+    const T* xp = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1;
+    T* op = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 * a.out.s1;
+    if (row[r] < 0) {  // padded batch row: zero output, state untouched
       float z[VEC];
 #pragma unroll
       for (int v = 0; v < VEC; ++v) z[v] = 0.f;
       for (int64_t t = 0; t < T_len; ++t) st_packet<T, VEC>(op + t * a.out.s2, pack<T, VEC>(z));
-      return;
+      continue;
     }
-    T* sp = static_cast<T*>(a.state.data) + row * a.state.s0 + d0 * a.state.s1;
-    const int64_t cache = a.cache_seqlens ? (int64_t)a.cache_seqlens[b * a.cache_stride] : 0;
-
-    // window = the W-1 history entries, then x
     float hw[W - 1][VEC];
 #pragma unroll
-    for (int i = 0; i < W - 1; ++i) {
-      const int64_t pos = a.cache_seqlens ? pos_mod(cache - (W - 1) + i, S) : S - (W - 1) + i;
-      unpack<T, VEC>(ld_packet<T, VEC>(sp + pos * a.state.s2), hw[i]);
-    }
+    for (int i = 0; i < W - 1; ++i) unpack<T, VEC>(hist[r][i], hw[i]);
     for (int64_t t = 0; t < T_len; ++t) {
       float xc[VEC];
-      unpack<T, VEC>(ld_packet<T, VEC>(xp + t * a.x.s2), xc);
+      unpack<T, VEC>(t == 0 ? x0[r] : ld_packet<T, VEC>(xp + t * a.x.s2), xc);
       float acc[VEC];
 #pragma unroll
       for (int v = 0; v < VEC; ++v) {
@@ -102,11 +126,22 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
 #pragma unroll
       for (int v = 0; v < VEC; ++v) hw[W - 2][v] = xc[v];
     }
+  }
 
-    // state write (raw copies, bit exact)
+  // phase 3: state writes (raw copies, bit exact)
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    if (!ok[r] || row[r] < 0) continue;
+    const T* xp = static_cast<const T*>(a.x.data) + (b0 + r) * a.x.s0 + d0 * a.x.s1;
+    T* sp = static_cast<T*>(a.state.data) + row[r] * a.state.s0 + d0 * a.state.s1;
     if (a.cache_seqlens) {
       for (int64_t t = 0; t < T_len; ++t)  // in order: with seqlen > state_len the last write wins
-        st_packet<T, VEC>(sp + pos_mod(cache + t, S) * a.state.s2, ld_packet<T, VEC>(xp + t * a.x.s2));
+        st_packet<T, VEC>(sp + pos_mod(cache[r] + t, S) * a.state.s2, t == 0 ? x0[r] : ld_packet<T, VEC>(xp + t * a.x.s2));
+    } else if (S == W - 1 && T_len == 1) {
+      // the whole old state is the history window: shift it from registers
+#pragma unroll
+      for (int i = 0; i + 1 < W - 1; ++i) st_packet<T, VEC>(sp + i * a.state.s2, hist[r][i + 1]);
+      st_packet<T, VEC>(sp + (S - 1) * a.state.s2, x0[r]);
     } else {
       // new[s] = old[s + T] (s + T < S) or x[s + T - S].  Positions move down, so a group
       // of G positions is read completely before it is written, in ascending groups.

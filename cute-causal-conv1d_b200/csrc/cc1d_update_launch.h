@@ -7,6 +7,8 @@
 
 namespace cc1d {
 
+constexpr int kUpdateRows = 4;  // batch rows per thread in the update kernel
+
 struct UpdateArgs {
   int64_t batch, dim, seqlen, state_len;
   TensorArg x, state, weight, bias, out;
