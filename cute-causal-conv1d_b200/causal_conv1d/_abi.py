@@ -68,11 +68,15 @@ class VarlenParams(ctypes.Structure):
     ]
 
 
+# Bytes of the library's static backward scratch array (CC1D_STATIC_SCRATCH_BYTES).
+STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
+
 # symbol -> (restype, argtypes); the same list is checked by the CPU test suite
 SIGNATURES = {
     "cc1d_fwd_launch": (c_i32, [ctypes.POINTER(FwdParams), c_void_p]),
     "cc1d_bwd_workspace_bytes": (c_i64, [ctypes.POINTER(BwdParams)]),
     "cc1d_bwd_launch": (c_i32, [ctypes.POINTER(BwdParams), c_void_p]),
+    "cc1d_bwd_launch_static": (c_i32, [ctypes.POINTER(BwdParams), c_void_p]),
     "cc1d_update_launch": (c_i32, [ctypes.POINTER(UpdateParams), c_void_p]),
     "cc1d_varlen_states_launch": (c_i32, [ctypes.POINTER(VarlenParams), c_void_p]),
     "cc1d_last_error": (ctypes.c_char_p, []),

@@ -301,6 +301,9 @@ cc1d_status check_conv_common(int64_t B, int64_t D, int64_t L, int64_t W, const 
 }
 
 }  // namespace
+
+void set_last_error(const char* msg) { g_last_error = msg; }
+
 }  // namespace cc1d
 
 using namespace cc1d;

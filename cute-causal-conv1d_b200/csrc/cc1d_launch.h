@@ -41,6 +41,9 @@ CC1D_DECLARE(fwd)
 CC1D_DECLARE(bwd)
 #undef CC1D_DECLARE
 
+// Sets the message returned by cc1d_last_error() on the calling thread.
+void set_last_error(const char* msg);
+
 cudaError_t rows_f32(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
 cudaError_t rows_f16(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
 cudaError_t rows_bf16(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);

@@ -132,6 +132,24 @@ int64_t cc1d_bwd_workspace_bytes(const cc1d_bwd_params* params);
 
 cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* params, void* stream);
 
+/* ----------------------------------------- backward without a caller workspace
+ * No counterpart in the reference.  For callers that cannot allocate device memory
+ * (plugin hosts that pass only the operands, servers with a fixed device-memory budget,
+ * code that must not touch the allocator between launches): same contract and results
+ * as cc1d_bwd_launch, but params->workspace and params->workspace_bytes are ignored and
+ * the scratch comes from a static array of CC1D_STATIC_SCRATCH_BYTES bytes inside the
+ * library, so the call allocates nothing.
+ *   - Every GPU on which the library is used holds the array until the process exits.
+ *   - The first call on a device looks up the array's device address there; make that
+ *     first call before capturing a stream.
+ *   - All calls share the array: calls that overlap on the GPU race on it.
+ *   - A problem needing more scratch than the array holds (cc1d_bwd_workspace_bytes)
+ *     is rejected with CC1D_ERR_VALUE before anything is launched.
+ */
+#define CC1D_STATIC_SCRATCH_BYTES (32 * 1024 * 1024)
+
+cc1d_status cc1d_bwd_launch_static(const cc1d_bwd_params* params, void* stream);
+
 /* -------------------------------------------------------------------- update
  * Replaces causal_conv1d/cutedsl_kernels.py:554-582 (causal_conv1d_update_cutedsl,
  * kernel :379-493) and the layout fallback causal_conv1d/cpp_functions.py:169-238;

@@ -23,6 +23,11 @@ def test_header_declares_the_bound_functions():
     assert declared_functions() == sorted(_abi.SIGNATURES)
 
 
+def test_static_scratch_size_matches_header():
+    m = re.search(r"#define CC1D_STATIC_SCRATCH_BYTES \((\d+) \* 1024 \* 1024\)", open(HEADER).read())
+    assert m and int(m.group(1)) * 1024 * 1024 == _abi.STATIC_SCRATCH_BYTES
+
+
 def test_library_exports_every_declared_symbol():
     lib = ctypes.CDLL(_abi.LIB_PATH)
     for name in declared_functions():
