@@ -356,7 +356,7 @@ def run_ours(args):
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": config_dict(world),
-        "roofline": {"bound": "hbm", "kernel": "bwd_channel_last (config 2)", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": "bwd_stream_kernel + reduce_unit_partials (config 2 backward)", "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": f"{peak_kind} hbm_gbs", "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": ncu_traffic("config2_bwd"),
                      "algorithmic_bytes": bb},

@@ -270,6 +270,10 @@ __global__ void __launch_bounds__(kThreads) bwd_channel_last_kernel(const ConvAr
 template <typename T, int W, int VEC, bool SILU, bool SEQ>
 struct BwdWalk {
   static constexpr int H = VEC / 2;
+  // 16-bit tensors with SiLU: wv/bv hold weight/2 and bias/2, so the running sum is
+  // h = p/2, g holds 2 * dout * silu'(p), dx = sum (w/2) g is exact, and the dweight /
+  // dbias sums carry a factor 2 that is removed when they are stored.
+  static constexpr bool HALF = SILU && sizeof(T) == 2;
   float2 wv[W][H], bv[H];
   float2 dw[W][H], db[H];
   float2 xw[W - 1][H], gw[W - 1][H];  // x and g at the W-1 rows before the current one
@@ -294,7 +298,8 @@ struct BwdWalk {
         }
         p = ffma2(wv[W - 1][i], xc[i], p);
         if constexpr (SEQ) p = (scur >= 0) ? p : make_float2(0.f, 0.f);
-        gv = fmul2(gv, silu_grad2(p));
+        if constexpr (HALF) gv = fmul2(gv, silu_grad_half_arg2_x2(p));
+        else gv = fmul2(gv, silu_grad2(p));
       }
       if constexpr (SEQ) gv = (scur >= 0) ? gv : make_float2(0.f, 0.f);
       g[i] = gv;
@@ -404,9 +409,10 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
       load_params<W, VEC>(a, d0, wf, bf);
 #pragma unroll
       for (int i = 0; i < H; ++i) {
-        st.bv[i] = make_float2(bf[2 * i], bf[2 * i + 1]);
+        constexpr float k = decltype(st)::HALF ? 0.5f : 1.0f;
+        st.bv[i] = make_float2(k * bf[2 * i], k * bf[2 * i + 1]);
 #pragma unroll
-        for (int w = 0; w < W; ++w) st.wv[w][i] = make_float2(wf[w][2 * i], wf[w][2 * i + 1]);
+        for (int w = 0; w < W; ++w) st.wv[w][i] = make_float2(k * wf[w][2 * i], k * wf[w][2 * i + 1]);
       }
     }
     const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
@@ -525,54 +531,92 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
 
   // ---- dweight / dbias: each warp unit writes its partial sums to its own slot; the
   // next kernel (reduce_unit_partials) adds the slots of each channel in unit order.
+  // The unit's slab is value-major ([VEC * (W + 1)][32 lanes]): each store below writes
+  // one 128-byte line.
   constexpr int PER_LANE = VEC * (W + 1);
-  float* mine = a.partials + (unit * 32 + lane) * PER_LANE;
+  constexpr float k = decltype(st)::HALF ? 0.5f : 1.0f;  // exact
+  float* mine = a.partials + unit * 32 * PER_LANE + lane;
 #pragma unroll
   for (int i = 0; i < H; ++i) {
 #pragma unroll
     for (int w = 0; w < W; ++w) {
-      mine[(2 * i) * (W + 1) + w] = st.dw[w][i].x;
-      mine[(2 * i + 1) * (W + 1) + w] = st.dw[w][i].y;
+      mine[((2 * i) * (W + 1) + w) * 32] = k * st.dw[w][i].x;
+      mine[((2 * i + 1) * (W + 1) + w) * 32] = k * st.dw[w][i].y;
     }
-    mine[(2 * i) * (W + 1) + W] = st.db[i].x;
-    mine[(2 * i + 1) * (W + 1) + W] = st.db[i].y;
+    mine[((2 * i) * (W + 1) + W) * 32] = k * st.db[i].x;
+    mine[((2 * i + 1) * (W + 1) + W) * 32] = k * st.db[i].y;
   }
 }
 
 // Deterministic sum of the warp-unit partials of the streamed backward kernels.  Slot
-// layout [unit][32 lanes][PER_LANE]; lane l of packet block pb covers channels
+// layout [unit][PER_LANE][32 lanes]; lane l of packet block pb covers channels
 // (pb*32 + l)*VEC .. +VEC-1 and PER_LANE = VEC*(W+1) values (W weights, then bias, per
-// channel).  One thread per (packet block, lane, value); the units of packet block pb
-// (all batch rows, all segments) are contiguous and are added in order with four
-// independent chains combined in a fixed order.
+// channel), so one unit's slots form a contiguous slab of 32*PER_LANE floats, and the
+// units of packet block pb (all batch rows, all segments) are contiguous.
+// A block owns one value index r of one packet block (32 lanes); each of its
+// kReduceChains warps adds every kReduceChains-th unit in unit order (loads issued four
+// at a time), and warp 0 adds the chains in chain order.  The order of every addition
+// depends only on the geometry, so the result is reproducible.
+constexpr int kReduceChains = 8;
+
 template <int W, int VEC>
-__global__ void __launch_bounds__(kThreads) reduce_unit_partials(const ConvArgs a) {
+__global__ void __launch_bounds__(32 * kReduceChains) reduce_unit_partials(const ConvArgs a) {
+  constexpr int PER_LANE = VEC * (W + 1);
+  constexpr int64_t SLAB = 32 * PER_LANE;
+  constexpr int S = kReduceChains;
+  __shared__ float chain_sum[S][32];
+  const int lane = threadIdx.x & 31;
+  const int chain = threadIdx.x >> 5;
+  const int64_t pb = blockIdx.x / PER_LANE;
+  const int r = static_cast<int>(blockIdx.x % PER_LANE);  // value index
+  const int q = r * 32 + lane;                            // slab position
+  grid_dependency_wait();  // the partials come from the kernel launched just before
+  const int64_t u0 = first_unit(a, pb * a.batch), u1 = first_unit(a, (pb + 1) * a.batch);
+  const float* src = a.partials + q;
+  float acc = 0.f;
+  int64_t k = u0 + chain;
+  for (; k + 3 * S < u1; k += 4 * S) {
+    const float v0 = __ldcg(src + (k + 0 * S) * SLAB);
+    const float v1 = __ldcg(src + (k + 1 * S) * SLAB);
+    const float v2 = __ldcg(src + (k + 2 * S) * SLAB);
+    const float v3 = __ldcg(src + (k + 3 * S) * SLAB);
+    acc += v0;
+    acc += v1;
+    acc += v2;
+    acc += v3;
+  }
+  for (; k < u1; k += S) acc += __ldcg(src + k * SLAB);
+  chain_sum[chain][lane] = acc;
+  __syncthreads();
+  if (chain != 0) return;
+  float sum = chain_sum[0][lane];
+#pragma unroll
+  for (int c = 1; c < S; ++c) sum += chain_sum[c][lane];
+  const int64_t d = (pb * 32 + lane) * VEC + r / (W + 1);
+  const int w = r % (W + 1);
+  if (d >= a.dim) return;
+  if (w < W) a.dweight[d * W + w] = sum;
+  else if (a.dbias) a.dbias[d] = sum;
+}
+
+// Launches reduce_unit_partials right behind the kernel that wrote the partials, as a
+// programmatic dependent launch: its blocks are scheduled as the writer's blocks retire
+// and wait in grid_dependency_wait() for the writer's results.
+template <int W, int VEC>
+static cudaError_t launch_reduce(const ConvArgs& a, cudaStream_t s) {
   constexpr int PER_LANE = VEC * (W + 1);
   const int64_t npb = (a.nv + 31) / 32;
-  const int64_t t = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  if (t >= npb * 32 * PER_LANE) return;
-  const int64_t pb = t / (32 * PER_LANE);
-  const int rem = static_cast<int>(t - pb * 32 * PER_LANE);
-  const int lane = rem / PER_LANE;
-  const int q = rem - lane * PER_LANE;
-  const int64_t d = (pb * 32 + lane) * VEC + q / (W + 1);
-  if (d >= a.dim) return;
-  const int w = q % (W + 1);
-  const int64_t u0 = first_unit(a, pb * a.batch), u1 = first_unit(a, (pb + 1) * a.batch);
-  const float* src = a.partials + rem;
-  const int64_t stride = 32 * PER_LANE;
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  int64_t k = u0;
-  for (; k + 4 <= u1; k += 4) {
-    s0 += __ldcg(src + (k + 0) * stride);
-    s1 += __ldcg(src + (k + 1) * stride);
-    s2 += __ldcg(src + (k + 2) * stride);
-    s3 += __ldcg(src + (k + 3) * stride);
-  }
-  for (; k < u1; ++k) s0 += __ldcg(src + k * stride);
-  const float s = (s0 + s1) + (s2 + s3);
-  if (w < W) a.dweight[d * W + w] = s;
-  else if (a.dbias) a.dbias[d] = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(npb * PER_LANE));
+  cfg.blockDim = dim3(32 * kReduceChains);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, reduce_unit_partials<W, VEC>, a);
 }
 
 // ------------------------------------------------------------------- rows
@@ -843,8 +887,7 @@ static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
 #undef CC1D_GO
       const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return e;
-      const int64_t n = ((a.nv + 31) / 32) * 32 * VEC * (W + 1);
-      reduce_unit_partials<W, VEC><<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, 0, s>>>(a);
+      return launch_reduce<W, VEC>(a, s);
     }
   } else if (ls.layout == kLayoutChannelLast) {
     constexpr int U = 2;
@@ -903,15 +946,12 @@ cudaError_t CC1D_DT_NAME(bwd)(const ConvArgs& a, const LaunchShape& ls, cudaStre
 
 // Sum of the row-stream kernel's warp-unit partials (one channel per lane: VEC = 1).
 cudaError_t CC1D_DT_NAME(reduce_rows)(const ConvArgs& a, int width, cudaStream_t s) {
-  const int64_t n = ((a.nv + 31) / 32) * 32 * (width + 1);
-  const unsigned grid = (unsigned)((n + kThreads - 1) / kThreads);
   switch (width) {
-    case 2: reduce_unit_partials<2, 1><<<grid, kThreads, 0, s>>>(a); break;
-    case 3: reduce_unit_partials<3, 1><<<grid, kThreads, 0, s>>>(a); break;
-    case 4: reduce_unit_partials<4, 1><<<grid, kThreads, 0, s>>>(a); break;
+    case 2: return launch_reduce<2, 1>(a, s);
+    case 3: return launch_reduce<3, 1>(a, s);
+    case 4: return launch_reduce<4, 1>(a, s);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 const void* CC1D_DT_NAME(bwd_kernel_ptr)(const LaunchShape& ls) {

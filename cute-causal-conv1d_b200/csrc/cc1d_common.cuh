@@ -136,6 +136,12 @@ __device__ __forceinline__ void cp_async_packet(void* smem_dst, const void* gsrc
   }
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel on its stream is still running;
+// this wait returns once that kernel has completed and its writes are visible.  For a
+// kernel launched without the attribute it returns at once.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
@@ -244,6 +250,17 @@ __device__ __forceinline__ float2 silu_grad2(float2 p) {
   const float2 d = fadd2(make_float2(1.0f, 1.0f), e);
   const float2 s = make_float2(rcp_approx(d.x), rcp_approx(d.y));
   return fmul2(s, ffma2(p, fmul2(e, s), make_float2(1.0f, 1.0f)));
+}
+
+// Twice d silu / dp of a pair whose argument was pre-scaled by 1/2 (h = p/2), one MUFU
+// per element: with t = tanh(h), sigmoid(p) = (1 + t)/2 and
+//   silu'(p) = sigmoid(p) * (1 + p * (1 - sigmoid(p))) = (1 + t) * (1 + h * (1 - t)) / 2.
+// Used for 16-bit tensors, whose outputs tolerate tanh.approx's error.
+__device__ __forceinline__ float2 silu_grad_half_arg2_x2(float2 h) {
+  const float2 t = make_float2(tanh_approx(h.x), tanh_approx(h.y));
+  const float2 one = make_float2(1.0f, 1.0f);
+  const float2 omt = ffma2(t, make_float2(-1.0f, -1.0f), one);  // 1 - t
+  return fmul2(fadd2(one, t), ffma2(h, omt, one));
 }
 
 // ------------------------------------------------------------- argument blocks

@@ -328,10 +328,11 @@ __global__ void __launch_bounds__(NT) bwd_rows_kernel(const ConvArgs a) {
   cp_async_wait<0>();
 
   // dweight / dbias partial sums of this warp unit (summed by reduce_unit_partials)
-  float* mine = a.partials + (unit * 32 + lane) * (W + 1);
+  // (slab of the unit: value-major, [W + 1][32 lanes], so every store is one 128-byte line)
+  float* mine = a.partials + unit * 32 * (W + 1) + lane;
 #pragma unroll
-  for (int w = 0; w < W; ++w) mine[w] = dw[w];
-  mine[W] = db;
+  for (int w = 0; w < W; ++w) mine[w * 32] = dw[w];
+  mine[W * 32] = db;
 }
 
 // ----------------------------------------------------------------- dispatch
