@@ -64,16 +64,20 @@ bool packet_ok_rows(const cc1d_tensor& t, int64_t B, int64_t D) {
 }
 
 // Packets of `bytes` along dim (channel-last) are legal for this (B, D, L) tensor.
+// The streamed kernels index warp units, columns and positions in 32 bits.
+constexpr int64_t kMax32 = (int64_t{1} << 31) - 1;
+
 bool stream_ok(const cc1d_tensor& t, int64_t B, int64_t dim, int64_t L, int bytes) {
   const int vec = bytes / elem_size(t.dtype);
   return t.stride[1] == 1 && dim % vec == 0 && (reinterpret_cast<uintptr_t>(t.data) % bytes) == 0 &&
-         stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[2], L, vec);
+         stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[2], L, vec) && L <= kMax32 && B * dim <= kMax32;
 }
 
 // (batch, dim, seqlen)-contiguous rows whose starts are 16-byte aligned.
-bool rows_stream_ok(const cc1d_tensor& t, int64_t B, int64_t D) {
+bool rows_stream_ok(const cc1d_tensor& t, int64_t B, int64_t D, int64_t L) {
   const int vec = 16 / elem_size(t.dtype);
-  return t.stride[2] == 1 && aligned16(t.data) && stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[1], D, vec);
+  return t.stride[2] == 1 && aligned16(t.data) && stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[1], D, vec) &&
+         L <= kMax32 && B * D <= kMax32;
 }
 
 int sm_count() {
@@ -418,8 +422,8 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
     *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }
-  if (p->x.stride[1] != 1 && rows_stream_ok(p->x, B, D) && rows_stream_ok(p->dout, B, D) &&
-      rows_stream_ok(p->dx, B, D)) {
+  if (p->x.stride[1] != 1 && rows_stream_ok(p->x, B, D, L) && rows_stream_ok(p->dout, B, D, L) &&
+      rows_stream_ok(p->dx, B, D, L)) {
     LaunchShape probe{};
     probe.layout = kLayoutRowStream;
     const size_t smem = (size_t)2 * kRowDepthBwd * kStreamThreads * 32;

@@ -309,33 +309,65 @@ __host__ __device__ inline int64_t first_unit(const ConvArgs& a, int64_t c) {
 }
 
 // The (column, segment) of warp unit u, the column's segment count and its first unit.
+// 32-bit arithmetic: the planners keep units, columns and seqlen below 2^31.
 struct WarpUnit {
   int64_t col, seg, nseg, first;
 };
-__device__ __forceinline__ WarpUnit warp_unit(const ConvArgs& a, int64_t u) {
+__device__ __forceinline__ WarpUnit warp_unit(const ConvArgs& a, int64_t unit) {
   WarpUnit w;
-  const int64_t q1 = a.seg_q + 1;
-  const int64_t big = a.seg_r * q1;
+  const unsigned u = static_cast<unsigned>(unit);
+  const unsigned q = static_cast<unsigned>(a.seg_q), q1 = q + 1u;
+  const unsigned big = static_cast<unsigned>(a.seg_r) * q1;
   if (u < big) {
-    w.col = u / q1;
-    w.seg = u - w.col * q1;
+    const unsigned c = u / q1;
+    w.col = c;
+    w.seg = u - c * q1;
     w.nseg = q1;
-    w.first = w.col * q1;
+    w.first = c * q1;
   } else {
-    const int64_t v = u - big;
-    const int64_t c = v / a.seg_q;
+    const unsigned v = u - big;
+    const unsigned c = v / q;
     w.col = a.seg_r + c;
-    w.seg = v - c * a.seg_q;
-    w.nseg = a.seg_q;
-    w.first = big + c * a.seg_q;
+    w.seg = v - c * q;
+    w.nseg = q;
+    w.first = big + c * q;
   }
   return w;
 }
 
+// Start of part s when len items are cut into n parts whose lengths differ by at most
+// one (the first len % n parts are one longer); s == n gives len.  32-bit arithmetic.
+__device__ __forceinline__ int64_t part_start(int64_t s, int64_t n, int64_t len) {
+  const unsigned un = static_cast<unsigned>(n), ul = static_cast<unsigned>(len), us = static_cast<unsigned>(s);
+  const unsigned base = ul / un, rem = ul - base * un;
+  return static_cast<int64_t>(us * base + min(us, rem));
+}
+
 // Weight and bias of VEC consecutive channels, as fp32.
+// fp32 (dim, W) weight with unit channel stride and fp32 unit-stride bias (or none) take
+// a branch-free path whose loads all issue back to back.
 template <int W, int VEC>
 __device__ __forceinline__ void load_params(const ConvArgs& a, int64_t d0, float (&wv)[W][VEC],
                                             float (&bv)[VEC]) {
+  const bool fast = d0 + VEC <= a.dim && a.weight.dtype == CC1D_FLOAT32 && a.weight.s1 == 1 &&
+                    (!a.bias.data || (a.bias.dtype == CC1D_FLOAT32 && a.bias.s0 == 1));
+  if (fast) {
+    const float* wp = static_cast<const float*>(a.weight.data) + d0 * a.weight.s0;
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+#pragma unroll
+      for (int w = 0; w < W; ++w) wv[w][v] = __ldg(wp + v * a.weight.s0 + w);
+    }
+    if (a.bias.data) {
+      const float* bp = static_cast<const float*>(a.bias.data) + d0;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) bv[v] = __ldg(bp + v);
+    } else {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) bv[v] = 0.f;
+    }
+    return;
+  }
 #pragma unroll
   for (int v = 0; v < VEC; ++v) {
     const int64_t d = d0 + v;
@@ -344,6 +376,40 @@ __device__ __forceinline__ void load_params(const ConvArgs& a, int64_t d0, float
     for (int w = 0; w < W; ++w)
       wv[w][v] = ok ? load_any(a.weight.data, a.weight.dtype, d * a.weight.s0 + w * a.weight.s1) : 0.f;
     bv[v] = (ok && a.bias.data) ? load_any(a.bias.data, a.bias.dtype, d * a.bias.s0) : 0.f;
+  }
+}
+
+// x at the W-1 rows before position l0 of one lane's VEC channels d0.. (rows before 0
+// come from initial_states, or are zero).  Away from position 0 all loads are issued
+// before any value is used.
+template <typename T, int W, int VEC>
+__device__ __forceinline__ void load_window(const ConvArgs& a, int64_t b, int64_t d0, int64_t l0,
+                                            float2 (&xw)[W - 1][VEC / 2]) {
+  constexpr int H = VEC / 2;
+  const T* col = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0;
+  if (l0 >= W - 1) {
+    Packet<T, VEC> raw[W - 1];
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k) raw[k] = ld_packet<T, VEC>(col + (l0 - (W - 1) + k) * a.x.s2);
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k) unpack2<T, VEC>(raw[k], xw[k]);
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < W - 1; ++k) {
+    const int64_t l = l0 - (W - 1) + k;
+    if (l >= 0) {
+      unpack2<T, VEC>(ld_packet<T, VEC>(col + l * a.x.s2), xw[k]);
+    } else if (a.init.data) {
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        const int64_t o = b * a.init.s0 + (d0 + 2 * i) * a.init.s1 + (W - 1 + l) * a.init.s2;
+        xw[k][i] = make_float2(load_any(a.init.data, a.init.dtype, o), load_any(a.init.data, a.init.dtype, o + a.init.s1));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < H; ++i) xw[k][i] = make_float2(0.f, 0.f);
+    }
   }
 }
 

@@ -141,12 +141,12 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   const int64_t unit = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
   if (unit >= a.units) return;
   const WarpUnit wu = warp_unit(a, unit);
-  const int64_t pb = wu.col / a.batch;  // packet block
+  const int64_t pb = static_cast<unsigned>(wu.col) / static_cast<unsigned>(a.batch);  // packet block
   const int64_t b = wu.col - pb * a.batch;
   const int64_t cv = pb * 32 + lane;
   const int64_t L = a.seqlen;
-  const int64_t l0 = wu.seg * L / wu.nseg;
-  const int64_t l1 = (wu.seg + 1) * L / wu.nseg;
+  const int64_t l0 = part_start(wu.seg, wu.nseg, L);
+  const int64_t l1 = part_start(wu.seg + 1, wu.nseg, L);
   if (cv >= a.nv || l0 >= l1) return;
   const int n = static_cast<int>(l1 - l0);
   const int64_t d0 = cv * VEC;
@@ -161,10 +161,13 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
     cp_async_commit();
   }
 
+  // parameter and window loads are all issued before the first use of either
   float2 wv[W][H], bv[H];
+  float2 xw[W - 1][H];
   {
     float wf[W][VEC], bf[VEC];
     load_params<W, VEC>(a, d0, wf, bf);
+    load_window<T, W, VEC>(a, b, d0, l0, xw);
     const float sc = HALF_ARG ? 0.5f : 1.0f;
 #pragma unroll
     for (int i = 0; i < H; ++i) {
@@ -174,26 +177,10 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
     }
   }
   const int* srow = SEQ ? static_cast<const int*>(a.seq_idx.data) + b * a.seq_idx.s0 : nullptr;
-
-  // window: rows l0-(W-1) .. l0-1 (initial states, or zeros, before position 0)
-  float2 xw[W - 1][H];
   int sw[W - 1];
 #pragma unroll
   for (int k = 0; k < W - 1; ++k) {
     const int64_t l = l0 - (W - 1) + k;
-    if (l >= 0) {
-      unpack2<T, VEC>(ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l * sx), xw[k]);
-    } else if (a.init.data) {
-#pragma unroll
-      for (int i = 0; i < H; ++i) {
-        const int64_t o = b * a.init.s0 + (d0 + 2 * i) * a.init.s1 + (W - 1 + l) * a.init.s2;
-        xw[k][i] = make_float2(load_any(a.init.data, a.init.dtype, o),
-                               load_any(a.init.data, a.init.dtype, o + a.init.s1));
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < H; ++i) xw[k][i] = make_float2(0.f, 0.f);
-    }
     sw[k] = (SEQ && l >= 0) ? srow[l * a.seq_idx.s1] : -1;
   }
 

@@ -100,12 +100,12 @@ template <int C>
 __device__ __forceinline__ RowLane row_lane(const ConvArgs& a, int64_t unit, int lane) {
   const WarpUnit wu = warp_unit(a, unit);
   RowLane r;
-  r.pb = wu.col / a.batch;
+  r.pb = static_cast<unsigned>(wu.col) / static_cast<unsigned>(a.batch);
   r.b = wu.col - r.pb * a.batch;
   r.d = r.pb * 32 + lane;
   const int64_t nsteps = (a.seqlen + C - 1) / C;
-  r.l0 = min(a.seqlen, (wu.seg * nsteps / wu.nseg) * C);
-  r.l1 = min(a.seqlen, ((wu.seg + 1) * nsteps / wu.nseg) * C);
+  r.l0 = min(a.seqlen, part_start(wu.seg, wu.nseg, nsteps) * C);
+  r.l1 = min(a.seqlen, part_start(wu.seg + 1, wu.nseg, nsteps) * C);
   r.active = r.d < a.dim && r.l0 < r.l1;
   return r;
 }
