@@ -239,7 +239,7 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   g.ls.packet = true;
   const int vec = 8 / es;  // both streamed kernels move 8-byte packets
   const int64_t nv = D / vec;
-  const int64_t warps_per_block = kStreamThreads / 32;
+  const int64_t warps_per_block = (bwd ? kBwdStreamThreads : kFwdStreamThreads) / 32;
   const int64_t ncol = B * ((nv + 31) / 32);
   const int64_t min_rows = bwd ? 32 : 16;
   const int64_t max_seg = std::max<int64_t>(1, L / min_rows);
@@ -253,7 +253,7 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   g.ntiles = (units + warps_per_block - 1) / warps_per_block;
   g.ncounters = 0;  // partials are summed by a second kernel
   g.partial_floats = units * 32 * vec * (width + 1);
-  g.ls.smem = bwd ? (size_t)kStreamDepth * kStreamThreads * 16 : (size_t)kStreamDepthFwd * kStreamThreads * 8;
+  g.ls.smem = bwd ? (size_t)kStreamDepth * kBwdStreamThreads * 16 : (size_t)kStreamDepthFwd * kFwdStreamThreads * 8;
   return g;
 }
 
@@ -356,8 +356,8 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
   if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->out, B, D, L, 8)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
-    const size_t smem = (size_t)kStreamDepthFwd * kStreamThreads * 8;
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), smem, kStreamThreads) * sm_count();
+    const size_t smem = (size_t)kStreamDepthFwd * kFwdStreamThreads * 8;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), smem, kFwdStreamThreads) * sm_count();
     g = plan_stream(false, B, D, L, W, es, resident);
   } else {
     if (p->x.stride[1] == 1 && p->out.stride[1] == 1) {
@@ -417,8 +417,9 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
   if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->dout, B, D, L, 8) && stream_ok(p->dx, B, D, L, 8)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
-    const size_t smem = (size_t)kStreamDepth * kStreamThreads * 16;
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kStreamThreads) * sm_count();
+    const size_t smem = (size_t)kStreamDepth * kBwdStreamThreads * 16;
+    probe.smem = smem;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kBwdStreamThreads) * sm_count();
     *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }

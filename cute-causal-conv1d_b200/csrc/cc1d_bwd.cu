@@ -12,6 +12,8 @@
 // the last CTA to finish a channel tile (arrival counted with one atomicAdd, no
 // waiting) sums the slots in slot order.  No float atomics anywhere, so results do
 // not depend on scheduling.  Compiled once per element type (CC1D_DT).
+#include <mutex>
+
 #include "cc1d_common.cuh"
 #include "cc1d_launch.h"
 
@@ -350,7 +352,9 @@ struct BwdWalk {
   }
 };
 
-// One wave of persistent warps (see WarpUnit): lane = one VEC-channel packet, warp =
+// One wave of persistent warps (see WarpUnit), one CTA of NT = 512 threads per SM (one
+// CTA of 16 warps keeps the warps' progress closer together than four CTAs of 4, whose
+// warps the scheduler serves by CTA age): lane = one VEC-channel packet, warp =
 // 32 consecutive packets of one batch row and one segment [l0, l1).  The x rows l0-(W-1) .. l0-1 (or initial states)
 // are read once into the window; x and dout rows l0 .. l1+W-2 stream through private
 // cp.async rings (zero filled past L, so g vanishes there without a check).  Row l
@@ -865,14 +869,39 @@ __global__ void __launch_bounds__(kThreads) bwd_row_kernel(const ConvArgs a) {
 }
 
 // ----------------------------------------------------------------- dispatch
+// Lets `kernel` use `bytes` of dynamic shared memory (above the 48 KB default) on the
+// current device; set once per kernel and device.
+static cudaError_t allow_smem(const void* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static struct Entry { const void* k; int dev; size_t bytes; } done[128];
+  static int n = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (done[i].k == kernel && done[i].dev == dev && done[i].bytes >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) return e;
+  if (n < 128) done[n++] = Entry{kernel, dev, bytes};
+  return cudaSuccess;
+}
+
 template <typename T, int W, int VEC>
 static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 8) {
-#define CC1D_GO(SI, SQ) bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kStreamThreads><<<ls.grid, kStreamThreads, ls.smem, s>>>(a)
-      if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
-      else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
+#define CC1D_GO(SI, SQ)                                                                               \
+  {                                                                                                   \
+    const auto kern = bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kBwdStreamThreads>;           \
+    const cudaError_t ea = allow_smem(reinterpret_cast<const void*>(kern), ls.smem);                   \
+    if (ea != cudaSuccess) return ea;                                                                 \
+    kern<<<ls.grid, kBwdStreamThreads, ls.smem, s>>>(a);                                              \
+  }
+      if (silu) { if (seq) CC1D_GO(true, true) else CC1D_GO(true, false) }
+      else { if (seq) CC1D_GO(false, true) else CC1D_GO(false, false) }
 #undef CC1D_GO
       const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return e;
@@ -919,8 +948,11 @@ static cudaError_t launch_bwd_t(const ConvArgs& a, const LaunchShape& ls, cudaSt
 template <typename T>
 static const void* bwd_kernel_ptr_t(const LaunchShape& ls) {
   constexpr int PV = 16 / sizeof(T);
-  if (ls.layout == kLayoutStream)
-    return reinterpret_cast<const void*>(bwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepth, kStreamThreads>);
+  if (ls.layout == kLayoutStream) {
+    const void* k = reinterpret_cast<const void*>(bwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepth, kBwdStreamThreads>);
+    allow_smem(k, ls.smem);  // so that the occupancy query sees the real limit
+    return k;
+  }
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(bwd_channel_last_kernel<T, 4, PV, true, false, 2>);
     return reinterpret_cast<const void*>(bwd_channel_last_kernel<T, 4, 1, true, false, 2>);

@@ -404,7 +404,7 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 8) {
-#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kStreamThreads><<<ls.grid, kStreamThreads, ls.smem, s>>>(a)
+#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kFwdStreamThreads><<<ls.grid, kFwdStreamThreads, ls.smem, s>>>(a)
       if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
       else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
 #undef CC1D_GO
@@ -453,7 +453,7 @@ static const void* fwd_kernel_ptr_t(const LaunchShape& ls) {
   // host uses this only for occupancy queries.
   constexpr int PV = 16 / sizeof(T);
   if (ls.layout == kLayoutStream)
-    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepthFwd, kStreamThreads>);
+    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepthFwd, kFwdStreamThreads>);
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, PV, true, false, 4>);
     return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, 1, true, false, 4>);
