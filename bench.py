@@ -140,7 +140,7 @@ def cpu_sample_rate(target_s: float, max_channels: int = CFG2["dim"]):
     from oracle import numpy_oracle as O
 
     c_oracle.build()
-    cores = c_oracle.max_threads()
+    cores = c_oracle.use_all_cores()
     b, L, W = CFG2["batch"], CFG2["seqlen"], CFG2["width"]
     rng = np.random.default_rng(0)
 
@@ -302,17 +302,28 @@ def run_ours(args):
         if world > 1:
             allreduce_param_grads(sets[kb]["bucket"])
 
-    # On one GPU a single graph holds NSETS consecutive steps, so that no graph-launch gap
-    # sits between the kernels of the timed steps; with N ranks each step ends in an
-    # eager NCCL all-reduce and steps replay one by one.
-    g_round = None
-    if world == 1:
-        g_round = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_round):
-            for i in range(NSETS):
-                fwd(i % NSETS)
-                bwd((i + NSETS // 2) % NSETS)
+    # One graph holds NSETS consecutive steps, so that no graph-launch gap sits between
+    # the kernels of the timed steps.  With N ranks each step's dweight|dbias all-reduce
+    # is captured on a side stream: it overlaps the next step's forward, and the graph
+    # joins it before it ends.
+    side = torch.cuda.Stream(dev) if world > 1 else None
+    if side is not None:
+        allreduce_param_grads(sets[0]["bucket"])  # communicator set up before capture
         torch.cuda.synchronize()
+    g_round = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_round):
+        cap = torch.cuda.current_stream()
+        for i in range(NSETS):
+            fwd(i % NSETS)
+            kb = (i + NSETS // 2) % NSETS
+            bwd(kb)
+            if side is not None:
+                side.wait_stream(cap)
+                with torch.cuda.stream(side):
+                    allreduce_param_grads(sets[kb]["bucket"])
+        if side is not None:
+            cap.wait_stream(side)
+    torch.cuda.synchronize()
 
     def run_steps(n):
         i = 0
@@ -387,7 +398,7 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
-        del g_fwd, g_bwd
+        del g_fwd, g_bwd, g_round
         dist.destroy_process_group()
     return 0
 

@@ -44,6 +44,13 @@ def max_threads() -> int:
     return int(load().cc1d_oracle_max_threads())
 
 
+def use_all_cores() -> int:
+    """Run the OpenMP loops on every core this process may use; returns that count."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    load().cc1d_oracle_set_threads(ctypes.c_int(n))
+    return max_threads()
+
+
 def _ptr(a):
     return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
 

@@ -181,3 +181,14 @@ int cc1d_oracle_max_threads(void) {
   return 1;
 #endif
 }
+
+/* Sets the OpenMP thread count of the calls above (launchers such as torchrun set
+ * OMP_NUM_THREADS=1 for every process; the CPU baseline wants every host core). */
+void cc1d_oracle_set_threads(int n) {
+#ifdef _OPENMP
+  extern void omp_set_num_threads(int);
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
