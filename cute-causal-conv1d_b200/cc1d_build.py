@@ -36,7 +36,7 @@ UNITS = [
     ("cc1d_static.cu", [], "cc1d_static.o"),
 ] + [
     (src, [f"-DCC1D_DT={dt}"], f"{src[:-3]}_{name}.o")
-    for src in ("cc1d_fwd.cu", "cc1d_bwd.cu", "cc1d_rows.cu")
+    for src in ("cc1d_fwd.cu", "cc1d_bwd.cu", "cc1d_rows.cu", "cc1d_rowwalk.cu")
     for dt, name in ((0, "f32"), (1, "f16"), (2, "bf16"))
 ]
 

@@ -112,6 +112,13 @@ int blocks_per_sm(const void* kernel, size_t smem, int threads = kThreads) {
 }
 
 const void* kernel_ptr(bool bwd, int dtype, const LaunchShape& ls) {
+  if (ls.layout == kLayoutRowWalk) {
+    switch (dtype) {
+      case CC1D_FLOAT32: return rowwalk_kernel_ptr_f32(bwd, ls.smem);
+      case CC1D_FLOAT16: return rowwalk_kernel_ptr_f16(bwd, ls.smem);
+      default: return rowwalk_kernel_ptr_bf16(bwd, ls.smem);
+    }
+  }
   if (ls.layout == kLayoutRowStream) {
     switch (dtype) {
       case CC1D_FLOAT32: return rows_kernel_ptr_f32(bwd);
@@ -127,6 +134,13 @@ const void* kernel_ptr(bool bwd, int dtype, const LaunchShape& ls) {
 }
 
 cudaError_t dispatch(bool bwd, int dtype, const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
+  if (ls.layout == kLayoutRowWalk) {
+    switch (dtype) {
+      case CC1D_FLOAT32: return rowwalk_f32(bwd, a, ls, s);
+      case CC1D_FLOAT16: return rowwalk_f16(bwd, a, ls, s);
+      default: return rowwalk_bf16(bwd, a, ls, s);
+    }
+  }
   if (ls.layout == kLayoutRowStream) {
     switch (dtype) {
       case CC1D_FLOAT32: return rows_f32(bwd, a, ls, s);
@@ -283,6 +297,38 @@ Geometry plan_rows(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es,
   return g;
 }
 
+// Row walk ((B, D, L) contiguous, lanes along the sequence): one wave of warps, each
+// walking an equal share of the rows x steps sequence (see cc1d_rowwalk.cu).
+Geometry plan_rowwalk(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_blocks) {
+  Geometry g;
+  std::memset(&g, 0, sizeof(g));
+  g.ls.width = width;
+  g.ls.layout = kLayoutRowWalk;
+  g.ls.packet = true;
+  const int64_t vec = 16 / es;
+  const int64_t steps = (L + 32 * vec - 1) / (32 * vec);
+  const int64_t total = B * D * steps;
+  const int64_t warps_per_block = kRowWalkThreads / 32;
+  const int64_t nw = std::max<int64_t>(1, std::min<int64_t>(resident_blocks * warps_per_block, total));
+  g.a.nck = steps;
+  g.a.units = total;
+  g.a.ncol = nw;
+  g.ntiles = (nw + warps_per_block - 1) / warps_per_block;
+  g.ncounters = 0;  // partials are summed by a second kernel
+  g.partial_floats = bwd ? (D + nw) * (width + 1) : 0;
+  g.ls.smem = (size_t)(bwd ? 2 : 1) * kRowWalkDepth * kRowWalkThreads * 16;
+  return g;
+}
+
+// (batch, dim, seqlen)-contiguous rows for the row walk: 16-byte aligned base and
+// strides, seqlen a whole number of packets, 32-bit step counts.
+bool rowwalk_ok(const cc1d_tensor& t, int64_t B, int64_t D, int64_t L) {
+  const int vec = 16 / elem_size(t.dtype);
+  const int64_t steps = (L + 32 * vec - 1) / (32 * vec);
+  return t.stride[2] == 1 && aligned16(t.data) && stride_ok(t.stride[0], B, vec) && stride_ok(t.stride[1], D, vec) &&
+         L % vec == 0 && B * D * steps <= kMax32;
+}
+
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 int64_t bwd_workspace_for(const Geometry& g) {
@@ -307,6 +353,23 @@ cc1d_status check_conv_common(int64_t B, int64_t D, int64_t L, int64_t W, const 
 }  // namespace
 
 void set_last_error(const char* msg) { g_last_error = msg; }
+
+cudaError_t allow_dynamic_smem(const void* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static struct Entry { const void* k; int dev; size_t bytes; } done[256];
+  static int n = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (done[i].k == kernel && done[i].dev == dev && done[i].bytes >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) return e;
+  if (n < 256) done[n++] = Entry{kernel, dev, bytes};
+  return cudaSuccess;
+}
 
 }  // namespace cc1d
 
@@ -359,6 +422,12 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
     const size_t smem = (size_t)kStreamDepthFwd * kFwdStreamThreads * 8;
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), smem, kFwdStreamThreads) * sm_count();
     g = plan_stream(false, B, D, L, W, es, resident);
+  } else if (!p->seq_idx.data && rowwalk_ok(p->x, B, D, L) && rowwalk_ok(p->out, B, D, L)) {
+    LaunchShape probe{};
+    probe.layout = kLayoutRowWalk;
+    probe.smem = (size_t)kRowWalkDepth * kRowWalkThreads * 16;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), probe.smem, kRowWalkThreads) * sm_count();
+    g = plan_rowwalk(false, B, D, L, W, es, resident);
   } else {
     if (p->x.stride[1] == 1 && p->out.stride[1] == 1) {
       packet = packet_ok_channel_last(p->x, B, D, L) && packet_ok_channel_last(p->out, B, D, L);
@@ -381,7 +450,7 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
   a.out = tensor_arg(p->out);
   g.ls.silu = p->silu != 0;
   g.ls.seq = p->seq_idx.data != nullptr;
-  if (g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream) {
+  if (g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream || g.ls.layout == kLayoutRowWalk) {
     g.ls.grid = dim3((unsigned)g.ntiles);
   } else {
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, g.ls), g.ls.smem) * sm_count();
@@ -421,6 +490,14 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
     probe.smem = smem;
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kBwdStreamThreads) * sm_count();
     *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
+    return CC1D_OK;
+  }
+  if (!p->seq_idx.data && rowwalk_ok(p->x, B, D, L) && rowwalk_ok(p->dout, B, D, L) && rowwalk_ok(p->dx, B, D, L)) {
+    LaunchShape probe{};
+    probe.layout = kLayoutRowWalk;
+    probe.smem = (size_t)2 * kRowWalkDepth * kRowWalkThreads * 16;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), probe.smem, kRowWalkThreads) * sm_count();
+    *out_g = plan_rowwalk(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }
   if (p->x.stride[1] != 1 && rows_stream_ok(p->x, B, D, L) && rows_stream_ok(p->dout, B, D, L) &&
@@ -501,7 +578,7 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
     e = cudaMemsetAsync(a.counters, 0, g.ncounters * sizeof(unsigned int), s);
     if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward counter reset");
   }
-  if (g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream) {
+  if (g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream || g.ls.layout == kLayoutRowWalk) {
     g.ls.grid = dim3((unsigned)g.ntiles);
   } else {
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, g.ls), g.ls.smem) * sm_count();
@@ -510,7 +587,7 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
   e = dispatch(true, p->x.dtype, a, g.ls, s);
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d backward launch");
   // the streamed layouts add a second kernel that sums the partials
-  g_launches.fetch_add(g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream ? 2 : 1);
+  g_launches.fetch_add(g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream || g.ls.layout == kLayoutRowWalk ? 2 : 1);
   return CC1D_OK;
 }
 

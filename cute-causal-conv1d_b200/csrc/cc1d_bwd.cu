@@ -12,8 +12,6 @@
 // the last CTA to finish a channel tile (arrival counted with one atomicAdd, no
 // waiting) sums the slots in slot order.  No float atomics anywhere, so results do
 // not depend on scheduling.  Compiled once per element type (CC1D_DT).
-#include <mutex>
-
 #include "cc1d_common.cuh"
 #include "cc1d_launch.h"
 
@@ -869,25 +867,6 @@ __global__ void __launch_bounds__(kThreads) bwd_row_kernel(const ConvArgs a) {
 }
 
 // ----------------------------------------------------------------- dispatch
-// Lets `kernel` use `bytes` of dynamic shared memory (above the 48 KB default) on the
-// current device; set once per kernel and device.
-static cudaError_t allow_smem(const void* kernel, size_t bytes) {
-  if (bytes <= 48 * 1024) return cudaSuccess;
-  static std::mutex mu;
-  static struct Entry { const void* k; int dev; size_t bytes; } done[128];
-  static int n = 0;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  std::lock_guard<std::mutex> lock(mu);
-  for (int i = 0; i < n; ++i)
-    if (done[i].k == kernel && done[i].dev == dev && done[i].bytes >= bytes) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e != cudaSuccess) return e;
-  if (n < 128) done[n++] = Entry{kernel, dev, bytes};
-  return cudaSuccess;
-}
-
 template <typename T, int W, int VEC>
 static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   const bool silu = ls.silu, seq = ls.seq;
@@ -896,7 +875,7 @@ static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
 #define CC1D_GO(SI, SQ)                                                                               \
   {                                                                                                   \
     const auto kern = bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kBwdStreamThreads>;           \
-    const cudaError_t ea = allow_smem(reinterpret_cast<const void*>(kern), ls.smem);                   \
+    const cudaError_t ea = allow_dynamic_smem(reinterpret_cast<const void*>(kern), ls.smem);                   \
     if (ea != cudaSuccess) return ea;                                                                 \
     kern<<<ls.grid, kBwdStreamThreads, ls.smem, s>>>(a);                                              \
   }
@@ -950,7 +929,7 @@ static const void* bwd_kernel_ptr_t(const LaunchShape& ls) {
   constexpr int PV = 16 / sizeof(T);
   if (ls.layout == kLayoutStream) {
     const void* k = reinterpret_cast<const void*>(bwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepth, kBwdStreamThreads>);
-    allow_smem(k, ls.smem);  // so that the occupancy query sees the real limit
+    allow_dynamic_smem(k, ls.smem);  // so that the occupancy query sees the real limit
     return k;
   }
   if (ls.layout == kLayoutChannelLast) {

@@ -20,6 +20,9 @@ constexpr int kFwdStreamThreads = 512; // CTA size of the streamed forward (one 
 constexpr int kBwdStreamThreads = 512; // CTA size of the streamed backward (one CTA per SM at 128 registers)
 constexpr int kLayoutRowStream = 3;    // (batch, dim, seqlen)-contiguous, per-lane sector stream
 constexpr int kRowDepthBwd = 4;        // row-stream backward: ring slots (32-byte sectors) per lane and tensor
+constexpr int kLayoutRowWalk = 4;      // (batch, dim, seqlen)-contiguous, lanes along the sequence
+constexpr int kRowWalkDepth = 8;       // row walk: ring slots (16-byte packets) per lane and tensor
+constexpr int kRowWalkThreads = 512;   // row walk: CTA size
 
 struct LaunchShape {
   dim3 grid;
@@ -52,6 +55,17 @@ cudaError_t rows_bf16(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_
 const void* rows_kernel_ptr_f32(bool bwd);
 const void* rows_kernel_ptr_f16(bool bwd);
 const void* rows_kernel_ptr_bf16(bool bwd);
+cudaError_t rowwalk_f32(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
+cudaError_t rowwalk_f16(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
+cudaError_t rowwalk_bf16(bool bwd, const ConvArgs&, const LaunchShape&, cudaStream_t);
+const void* rowwalk_kernel_ptr_f32(bool bwd, size_t smem);
+const void* rowwalk_kernel_ptr_f16(bool bwd, size_t smem);
+const void* rowwalk_kernel_ptr_bf16(bool bwd, size_t smem);
+
+// Lets `kernel` use `bytes` of dynamic shared memory (above the 48 KB default) on the
+// current device; the attribute is set once per kernel and device.
+cudaError_t allow_dynamic_smem(const void* kernel, size_t bytes);
+
 cudaError_t reduce_rows_f32(const ConvArgs&, int width, cudaStream_t);
 cudaError_t reduce_rows_f16(const ConvArgs&, int width, cudaStream_t);
 cudaError_t reduce_rows_bf16(const ConvArgs&, int width, cudaStream_t);
