@@ -134,16 +134,60 @@ __device__ __forceinline__ void lane_window(const float (&xe)[VEC], float (&carr
   for (int j = 0; j < W - 1; ++j) carry[j] = __shfl_sync(FULL, xe[VEC - (W - 1) + j], 31);
 }
 
+// Producer side of the walk: streams this lane's packet of consecutive steps (running
+// across rows) into a ring of P slots, zero-filling past the range and past the row end.
+template <typename T, int VEC, int P, int NT, int NTENS>
+struct WalkFeed {
+  static constexpr int S = 32 * VEC;
+  const TensorArg* tens[NTENS];
+  Packet<T, VEC>* ring[NTENS];  // slot 0 of this thread's ring in each tensor
+  const T* src[NTENS];          // this lane's packet of the next step
+  int64_t pos;                  // its position in the row
+  int step, b, d, slot, left;
+
+  __device__ __forceinline__ void start(const ConvArgs& a, const RowCursor& c, int lane, int count) {
+    step = c.step;
+    b = c.b;
+    d = c.d;
+    slot = 0;
+    left = count;
+    pos = (int64_t)step * S + lane * VEC;
+#pragma unroll
+    for (int t = 0; t < NTENS; ++t) src[t] = static_cast<const T*>(tens[t]->data) + (int64_t)b * tens[t]->s0 + (int64_t)d * tens[t]->s1 + pos;
+  }
+  __device__ __forceinline__ void issue(const ConvArgs& a, int lane) {
+    const bool ok = left > 0 && pos < a.seqlen;
+#pragma unroll
+    for (int t = 0; t < NTENS; ++t) cp_async_packet<sizeof(Packet<T, VEC>)>(ring[t] + slot * NT, src[t], ok);
+    cp_async_commit();
+    --left;
+    slot = slot + 1 == P ? 0 : slot + 1;
+    pos += S;
+#pragma unroll
+    for (int t = 0; t < NTENS; ++t) src[t] += S;
+    if (++step == a.nck) {  // next row
+      step = 0;
+      if (++b == a.batch) {
+        b = 0;
+        ++d;
+      }
+      pos = lane * VEC;
+#pragma unroll
+      for (int t = 0; t < NTENS; ++t) src[t] = static_cast<const T*>(tens[t]->data) + (int64_t)b * tens[t]->s0 + (int64_t)d * tens[t]->s1 + pos;
+    }
+  }
+};
+
 // ------------------------------------------------------------------- forward
 // STATES: initial_states and/or final_states are given (compiled out otherwise).
 template <typename T, int W, bool SILU, bool STATES, int P, int NT>
 __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
   constexpr int VEC = 16 / sizeof(T);
+  constexpr int H2 = VEC / 2;
   constexpr int S = 32 * VEC;
   constexpr bool HALF_ARG = SILU && !std::is_same<T, float>::value;
   using Pk = Packet<T, VEC>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  Pk* ring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
   if (warp >= a.ncol) return;
@@ -152,25 +196,16 @@ __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
   const int n = static_cast<int>(q1 - q0);
   const int64_t L = a.seqlen;
 
-  RowCursor pc = cursor_at(a, q0);
-  auto prefetch = [&](int j, int slot) {
-    const int64_t pos = (int64_t)pc.step * S + lane * VEC;
-    cp_async_packet<sizeof(Pk)>(ring + slot * NT, row_of<const T>(a.x, pc) + pos, j < n && pos < L);
-    cp_async_commit();
-    cp_async_wait<P - 1>();
-    cursor_next(pc, a);
-  };
+  RowCursor cc = cursor_at(a, q0);
+  WalkFeed<T, VEC, P, NT, 1> feed;
+  feed.tens[0] = &a.x;
+  feed.ring[0] = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
+  feed.start(a, cc, lane, n);
 #pragma unroll
-  for (int j = 0; j < P - 1; ++j) {
-    const int64_t pos = (int64_t)pc.step * S + lane * VEC;
-    cp_async_packet<sizeof(Pk)>(ring + j * NT, row_of<const T>(a.x, pc) + pos, j < n && pos < L);
-    cp_async_commit();
-    cursor_next(pc, a);
-  }
+  for (int j = 0; j < P - 1; ++j) feed.issue(a, lane);
 
   // Row-boundary values are loaded one row (initial states) or one channel (weights)
   // ahead, so that no load latency sits on the walk.
-  RowCursor cc = cursor_at(a, q0);
   const float sc = HALF_ARG ? 0.5f : 1.0f;
   float wv[W], bv, wn[W], bn;
   int cur_d = cc.d;
@@ -180,8 +215,11 @@ __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
   row_halo<T, W>(a, cc, (int64_t)cc.step * S, carry);
   if constexpr (STATES) row_init<W>(a, row_after(a, cc), ninit);
 
-  bool started = false;  // the first step's row values come from the prologue
-  auto step = [&](const Pk& raw) {
+  const Pk* ring = feed.ring[0];
+  int slot = 0;
+  int left = n;
+  bool started = false;  // the first row's values come from the prologue
+  while (left > 0) {
     if (cc.step == 0 && started) {  // a new row: take the values loaded ahead
 #pragma unroll
       for (int j = 0; j < W - 1; ++j) carry[j] = STATES ? ninit[j] : 0.f;
@@ -195,46 +233,56 @@ __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
       }
     }
     started = true;
-    float xe[VEC], xs[VEC + W - 1];
-    unpack<T, VEC>(raw, xe);
-    lane_window<W, VEC>(xe, carry, lane, xs);
-    float2 o2[VEC / 2];
+    const int seg = min(static_cast<int>(a.nck) - cc.step, left);
+    const bool row_ends = cc.step + seg == a.nck;
+    int64_t pos = (int64_t)cc.step * S + lane * VEC;
+    T* po = row_of<T>(a.out, cc) + pos;
+#pragma unroll 2
+    for (int k = 0; k < seg; ++k) {
+      feed.issue(a, lane);
+      cp_async_wait<P - 1>();
+      float xe[VEC], xs[VEC + W - 1];
+      unpack<T, VEC>(ring[slot * NT], xe);
+      slot = slot + 1 == P ? 0 : slot + 1;
+      lane_window<W, VEC>(xe, carry, lane, xs);
+      // fp32 pairs hold elements (m, m + VEC/2): a window shifted by w is again a pair
+      // of the same layout, so no register has to be moved to form FFMA2 operands
+      float o[VEC];
 #pragma unroll
-    for (int m = 0; m < VEC / 2; ++m) {
-      float2 s = make_float2(bv, bv);
+      for (int m = 0; m < H2; ++m) {
+        float2 s = make_float2(bv, bv);
 #pragma unroll
-      for (int w = 0; w < W; ++w) s = ffma2(make_float2(wv[w], wv[w]), make_float2(xs[2 * m + w], xs[2 * m + 1 + w]), s);
-      if constexpr (HALF_ARG) s = silu_half_arg2(s);
-      else if constexpr (SILU) s = silu_exact2(s);
-      o2[m] = s;
+        for (int w = 0; w < W; ++w) s = ffma2(make_float2(wv[w], wv[w]), make_float2(xs[m + w], xs[m + H2 + w]), s);
+        if constexpr (HALF_ARG) s = silu_half_arg2(s);
+        else if constexpr (SILU) s = silu_exact2(s);
+        o[m] = s.x;
+        o[m + H2] = s.y;
+      }
+      if (pos < L) st_packet<T, VEC>(po, pack<T, VEC>(o));
+      // final states: the last W-1 entries of x (seqlen is a whole number of packets >=
+      // W-1, so they sit at the end of one lane's packet of the row's last step)
+      if (STATES && a.final_states.data && row_ends && k == seg - 1) {
+        const int src = static_cast<int>(((L - 1) % S) / VEC);
+        float f[W - 1];
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j) f[j] = __shfl_sync(0xffffffffu, xe[VEC - (W - 1) + j], src);
+        if (lane < W - 1)
+          store_any(a.final_states.data, a.final_states.dtype,
+                    (int64_t)cc.b * a.final_states.s0 + (int64_t)cc.d * a.final_states.s1 + lane * a.final_states.s2,
+                    select_of<W - 1>(f, lane));
+      }
+      pos += S;
+      po += S;
     }
-    const int64_t pos = (int64_t)cc.step * S + lane * VEC;
-    if (pos < L) st_packet<T, VEC>(row_of<T>(a.out, cc) + pos, pack2<T, VEC>(o2));
-    // final states: the last W-1 entries of x (seqlen is a whole number of packets >= W-1,
-    // so they sit at the end of one lane's packet of the row's last step)
-    if (STATES && a.final_states.data && cc.step == a.nck - 1) {
-      const int src = static_cast<int>(((L - 1) % S) / VEC);
-      float f[W - 1];
-#pragma unroll
-      for (int j = 0; j < W - 1; ++j) f[j] = __shfl_sync(0xffffffffu, xe[VEC - (W - 1) + j], src);
-      if (lane < W - 1)
-        store_any(a.final_states.data, a.final_states.dtype,
-                  (int64_t)cc.b * a.final_states.s0 + (int64_t)cc.d * a.final_states.s1 + lane * a.final_states.s2, select_of<W - 1>(f, lane));
+    left -= seg;
+    cc.step += seg;
+    if (cc.step == a.nck) {
+      cc.step = 0;
+      if (++cc.b == a.batch) {
+        cc.b = 0;
+        ++cc.d;
+      }
     }
-    cursor_next(cc, a);
-  };
-
-  int j = 0;
-  for (; j + P <= n; j += P) {
-#pragma unroll
-    for (int u = 0; u < P; ++u) {
-      prefetch(j + u + P - 1, (u + P - 1) % P);
-      step(ring[u * NT]);
-    }
-  }
-  for (; j < n; ++j) {
-    prefetch(j + P - 1, (j + P - 1) % P);
-    step(ring[(j % P) * NT]);
   }
   cp_async_wait<0>();
 }
@@ -244,6 +292,7 @@ __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
 template <typename T, int W, bool SILU, bool STATES, int P, int NT>
 __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
   constexpr int VEC = 16 / sizeof(T);
+  constexpr int H2 = VEC / 2;  // fp32 pairs hold elements (m, m + H2), as in the forward
   constexpr int S = 32 * VEC;
   constexpr unsigned FULL = 0xffffffffu;
   // 16-bit tensors with SiLU: weights and bias are halved, the running sum is h = p/2
@@ -252,36 +301,27 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
   constexpr bool HALF = SILU && sizeof(T) == 2;
   using Pk = Packet<T, VEC>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  Pk* xring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
-  Pk* gring = reinterpret_cast<Pk*>(smem_raw) + P * NT + threadIdx.x;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
   if (warp >= a.ncol) return;
   const int64_t q0 = part_start(warp, a.ncol, a.units), q1 = part_start(warp + 1, a.ncol, a.units);
   if (q0 >= q1) return;
-  const int n = static_cast<int>(q1 - q0);                      // steps that accumulate
-  const int nall = n + ((q1 % a.nck) != 0 ? 1 : 0);             // plus the right-halo step
+  const int n = static_cast<int>(q1 - q0);  // steps that accumulate
+  const bool halo_step = (q1 % a.nck) != 0; // the range ends inside a row: one more step
   const int64_t L = a.seqlen;
 
-  RowCursor pc = cursor_at(a, q0);
-  auto issue = [&](int j, int slot) {
-    const int64_t pos = (int64_t)pc.step * S + lane * VEC;
-    const bool ok = j < nall && pos < L;
-    cp_async_packet<sizeof(Pk)>(xring + slot * NT, row_of<const T>(a.x, pc) + pos, ok);
-    cp_async_packet<sizeof(Pk)>(gring + slot * NT, row_of<const T>(a.dout, pc) + pos, ok);
-    cp_async_commit();
-    cursor_next(pc, a);
-  };
+  RowCursor cc = cursor_at(a, q0);
+  WalkFeed<T, VEC, P, NT, 2> feed;
+  feed.tens[0] = &a.x;
+  feed.tens[1] = &a.dout;
+  feed.ring[0] = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
+  feed.ring[1] = reinterpret_cast<Pk*>(smem_raw) + P * NT + threadIdx.x;
+  feed.start(a, cc, lane, n + (halo_step ? 1 : 0));
 #pragma unroll
-  for (int j = 0; j < P - 1; ++j) issue(j, j);
-  auto prefetch = [&](int j, int slot) {
-    issue(j, slot);
-    cp_async_wait<P - 1>();
-  };
+  for (int j = 0; j < P - 1; ++j) feed.issue(a, lane);
 
   // Row-boundary values are loaded one row (initial states, dfinal_states) or one
   // channel (weights) ahead, so that no load latency sits on the walk.
-  RowCursor cc = cursor_at(a, q0);
   constexpr float sc = HALF ? 0.5f : 1.0f;
   float wv[W], bv, wn[W], bn;
   int cur_d = cc.d;
@@ -299,8 +339,6 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
       dfin[j] = a.dfinal.data ? load_any(a.dfinal.data, a.dfinal.dtype, (int64_t)c.b * a.dfinal.s0 + (int64_t)c.d * a.dfinal.s1 + j * a.dfinal.s2) : 0.f;
   };
   if constexpr (STATES) row_dfinal(cc);
-  float gprev[VEC];
-  bool have_prev = false;
 
   // this warp's (channel, range) piece of dweight/dbias
   auto flush = [&](int64_t d) {
@@ -323,9 +361,10 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
     db = make_float2(0.f, 0.f);
   };
 
-  // dx of the step at `rc` (g values gs) given the first W-1 g values of the step to its
-  // right (nxt, read from lane 0); adds dfinal_states on the row's last step.
-  auto emit = [&](const RowCursor& rc, const float (&gs)[VEC], const float (&nxt)[VEC]) {
+  // dx of one step (g values gs, lane position pos, output pdx) given the first W-1 g
+  // values of the step to its right (nxt, read from lane 0); on the row's last step
+  // (last) it adds dfinal_states.
+  auto emit = [&](T* pdx, int64_t pos, const float (&gs)[VEC], const float (&nxt)[VEC], bool last) {
     float G[VEC + W - 1];
 #pragma unroll
     for (int i = 0; i < VEC; ++i) G[i] = gs[i];
@@ -335,33 +374,56 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
       const float h = __shfl_sync(FULL, nxt[j], 0);
       G[VEC + j] = lane == 31 ? h : v;
     }
-    float2 dx2[VEC / 2];
+    float dxe[VEC];
 #pragma unroll
-    for (int m = 0; m < VEC / 2; ++m) {
+    for (int m = 0; m < H2; ++m) {
       float2 s = make_float2(0.f, 0.f);
 #pragma unroll
       for (int w = 0; w < W; ++w)
-        s = ffma2(make_float2(wv[w], wv[w]), make_float2(G[2 * m + W - 1 - w], G[2 * m + 1 + W - 1 - w]), s);
-      dx2[m] = s;
+        s = ffma2(make_float2(wv[w], wv[w]), make_float2(G[m + W - 1 - w], G[m + H2 + W - 1 - w]), s);
+      dxe[m] = s.x;
+      dxe[m + H2] = s.y;
     }
-    const int64_t pos = (int64_t)rc.step * S + lane * VEC;
-    if (STATES && a.dfinal.data && rc.step == a.nck - 1) {  // dfin: this row's dfinal_states
+    if (STATES && last && a.dfinal.data) {  // dfin: this row's dfinal_states
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
         const int64_t jj = pos + e - (L - (W - 1));  // index into dfinal_states
-        if (jj >= 0 && jj < W - 1) {
-          const float v = select_of<W - 1>(dfin, jj);
-          if (e & 1) dx2[e >> 1].y += v;
-          else dx2[e >> 1].x += v;
-        }
+        if (jj >= 0 && jj < W - 1) dxe[e] += select_of<W - 1>(dfin, jj);
       }
     }
-    if (pos < L) st_packet<T, VEC>(row_of<T>(a.dx, rc) + pos, pack2<T, VEC>(dx2));
+    if (pos < L) st_packet<T, VEC>(pdx, pack<T, VEC>(dxe));
   };
 
-  RowCursor prev_c = cc;
-  bool started = false;  // the first step's row values come from the prologue
-  auto step = [&](const Pk& rx, const Pk& rg, bool real) {
+  // g of the next ring slot (and its x window)
+  const Pk* xring = feed.ring[0];
+  const Pk* gring = feed.ring[1];
+  int slot = 0;
+  auto next_g = [&](float (&xs)[VEC + W - 1], float (&g)[VEC]) {
+    feed.issue(a, lane);
+    cp_async_wait<P - 1>();
+    float xe[VEC], de[VEC];
+    unpack<T, VEC>(xring[slot * NT], xe);
+    unpack<T, VEC>(gring[slot * NT], de);
+    slot = slot + 1 == P ? 0 : slot + 1;
+    lane_window<W, VEC>(xe, carry, lane, xs);
+#pragma unroll
+    for (int m = 0; m < H2; ++m) {
+      float2 gv = make_float2(de[m], de[m + H2]);
+      if constexpr (SILU) {
+        float2 s = make_float2(bv, bv);
+#pragma unroll
+        for (int w = 0; w < W; ++w) s = ffma2(make_float2(wv[w], wv[w]), make_float2(xs[m + w], xs[m + H2 + w]), s);
+        if constexpr (HALF) gv = fmul2(gv, silu_grad_half_arg2_x2(s));
+        else gv = fmul2(gv, silu_grad2(s));
+      }
+      g[m] = gv.x;
+      g[m + H2] = gv.y;
+    }
+  };
+
+  int left = n;
+  bool started = false;  // the first row's values come from the prologue
+  while (left > 0) {
     if (cc.step == 0 && started) {  // a new row: take the values loaded ahead
 #pragma unroll
       for (int j = 0; j < W - 1; ++j) carry[j] = STATES ? ninit[j] : 0.f;
@@ -379,71 +441,54 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
       }
     }
     started = true;
-    float xe[VEC], de[VEC], xs[VEC + W - 1], g[VEC];
-    unpack<T, VEC>(rx, xe);
-    unpack<T, VEC>(rg, de);
-    lane_window<W, VEC>(xe, carry, lane, xs);
+    const int seg = min(static_cast<int>(a.nck) - cc.step, left);
+    const bool row_ends = cc.step + seg == a.nck;
+    int64_t pos = (int64_t)cc.step * S + lane * VEC;
+    T* pdx = row_of<T>(a.dx, cc) + pos;
+    float gprev[VEC];
+    for (int k = 0; k < seg; ++k) {
+      float xs[VEC + W - 1], g[VEC];
+      next_g(xs, g);
+      if (k > 0) emit(pdx - S, pos - S, gprev, g, false);
+      // dinitial_states: dx at positions -(W-1) .. -1 of the row, from g at 0 .. W-2
+      if (STATES && k == 0 && cc.step == 0 && a.dinit.data && lane == 0) {
 #pragma unroll
-    for (int m = 0; m < VEC / 2; ++m) {
-      float2 gv = make_float2(de[2 * m], de[2 * m + 1]);
-      if constexpr (SILU) {
-        float2 s = make_float2(bv, bv);
+        for (int kk = 0; kk < W - 1; ++kk) {
+          float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < W; ++w) s = ffma2(make_float2(wv[w], wv[w]), make_float2(xs[2 * m + w], xs[2 * m + 1 + w]), s);
-        if constexpr (HALF) gv = fmul2(gv, silu_grad_half_arg2_x2(s));
-        else gv = fmul2(gv, silu_grad2(s));
+          for (int w = 0; w <= kk; ++w) v = fmaf(wv[w], g[kk - w], v);
+          store_any(a.dinit.data, a.dinit.dtype, (int64_t)cc.b * a.dinit.s0 + (int64_t)cc.d * a.dinit.s1 + kk * a.dinit.s2, v);
+        }
       }
-      g[2 * m] = gv.x;
-      g[2 * m + 1] = gv.y;
-    }
-    if (have_prev) emit(prev_c, gprev, g);
-    // dinitial_states: dx at positions -(W-1) .. -1 of the row, from g at 0 .. W-2
-    if (STATES && cc.step == 0 && a.dinit.data && lane == 0) {
 #pragma unroll
-      for (int k = 0; k < W - 1; ++k) {
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w <= k; ++w) v = fmaf(wv[w], g[k - w], v);
-        store_any(a.dinit.data, a.dinit.dtype, (int64_t)cc.b * a.dinit.s0 + (int64_t)cc.d * a.dinit.s1 + k * a.dinit.s2, v);
-      }
-    }
-    if (real) {
-#pragma unroll
-      for (int m = 0; m < VEC / 2; ++m) {
-        const float2 gm = make_float2(g[2 * m], g[2 * m + 1]);
+      for (int m = 0; m < H2; ++m) {
+        const float2 gm = make_float2(g[m], g[m + H2]);
         db = fadd2(db, gm);
 #pragma unroll
-        for (int w = 0; w < W; ++w) dw[w] = ffma2(gm, make_float2(xs[2 * m + w], xs[2 * m + 1 + w]), dw[w]);
+        for (int w = 0; w < W; ++w) dw[w] = ffma2(gm, make_float2(xs[m + w], xs[m + H2 + w]), dw[w]);
       }
-      if (cc.step == a.nck - 1) {  // row end: nothing to the right
-        float zero[VEC];
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) zero[i] = 0.f;
-        emit(cc, g, zero);
-        have_prev = false;
-      } else {
+      for (int i = 0; i < VEC; ++i) gprev[i] = g[i];
+      pos += S;
+      pdx += S;
+    }
+    left -= seg;
+    if (row_ends) {  // nothing right of the row's last step
+      float zero[VEC];
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) gprev[i] = g[i];
-        prev_c = cc;
-        have_prev = true;
+      for (int i = 0; i < VEC; ++i) zero[i] = 0.f;
+      emit(pdx - S, pos - S, gprev, zero, true);
+      cc.step = 0;
+      if (++cc.b == a.batch) {
+        cc.b = 0;
+        ++cc.d;
       }
-    } else {
-      have_prev = false;  // the right-halo step only fed the emission above
+    } else {  // the range ends inside the row: the right-halo step supplies g
+      float xs[VEC + W - 1], g[VEC];
+      next_g(xs, g);
+      emit(pdx - S, pos - S, gprev, g, false);
+      cc.step += seg;
     }
-    cursor_next(cc, a);
-  };
-
-  int j = 0;
-  for (; j + P <= nall; j += P) {
-#pragma unroll
-    for (int u = 0; u < P; ++u) {
-      prefetch(j + u + P - 1, (u + P - 1) % P);
-      step(xring[u * NT], gring[u * NT], j + u < n);
-    }
-  }
-  for (; j < nall; ++j) {
-    prefetch(j + P - 1, (j + P - 1) % P);
-    step(xring[(j % P) * NT], gring[(j % P) * NT], j < n);
   }
   cp_async_wait<0>();
   flush(cur_d);
