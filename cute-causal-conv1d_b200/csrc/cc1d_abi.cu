@@ -598,6 +598,8 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   if (B < 0 || D < 0 || T < 0 || S < 0 || p->state_batch < 0) return fail(CC1D_ERR_VALUE, "sizes must be >= 0");
   if (W < 2 || W > 4) return fail(CC1D_ERR_VALUE, "width must be 2, 3, or 4");
   if (S < W - 1) return fail(CC1D_ERR_VALUE, "conv_state is shorter than the convolution history");
+  if (B > kMax32 || T > kMax32 || S > kMax32 || p->state_batch > kMax32)
+    return fail(CC1D_ERR_VALUE, "update sizes must be below 2^31");
   if (!is_float(p->x.dtype)) return fail(CC1D_ERR_TYPE, "x must be float32, float16, or bfloat16");
   if (!is_float(p->weight.dtype)) return fail(CC1D_ERR_TYPE, "weight must be a float tensor");
   if (p->bias.data && !is_float(p->bias.dtype)) return fail(CC1D_ERR_TYPE, "bias must be a float tensor");

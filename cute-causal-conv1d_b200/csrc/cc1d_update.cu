@@ -14,16 +14,13 @@
 
 namespace cc1d {
 
-__device__ __forceinline__ int64_t pos_mod(int64_t v, int64_t m) {
-  int64_t r = v % m;
-  return r < 0 ? r + m : r;
-}
-
 template <typename T, int W, int VEC>
 __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
   // CTA tile: 32 channel packets x (8 warps x BR batch rows).  A thread owns one packet
   // for BR batch rows: it loads the weights once, issues the loads of all BR rows before
   // using any of them (the rows' memory latencies overlap), then computes and writes.
+  // Positions inside a state row are 32-bit: the circular base cache % state_len is taken
+  // once per row and every later position is one add and one wrap.
   constexpr int BR = kUpdateRows;
   const int tx = threadIdx.x & 31;
   const int ty = threadIdx.x >> 5;
@@ -33,8 +30,21 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
   const int64_t b0 = ((blockIdx.x / nbx) * 8 + ty) * BR;
   if (cv >= nv || b0 >= a.batch) return;
   const int64_t d0 = cv * VEC;
-  const int64_t T_len = a.seqlen;
-  const int64_t S = a.state_len;
+  const int T_len = static_cast<int>(a.seqlen);
+  const int S = static_cast<int>(a.state_len);
+
+  // phase 1: first inputs and row indices (independent loads, issued first)
+  int row[BR], base[BR];
+  bool ok[BR];
+  Packet<T, VEC> hist[BR][W - 1], x0[BR];
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    const int64_t b = b0 + r;
+    ok[r] = b < a.batch;
+    if (ok[r]) x0[r] = ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1);
+    row[r] = (ok[r] && a.indices) ? a.indices[b * a.indices_stride] : static_cast<int>(b);
+    base[r] = (ok[r] && a.cache_seqlens) ? a.cache_seqlens[b * a.cache_stride] : 0;
+  }
 
   float wv[W][VEC], bv[VEC];
   if (a.weight_vec) {  // contiguous fp32 (dim, W): this thread's VEC*W weights are adjacent
@@ -52,6 +62,12 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
     for (int v = 0; v < VEC; ++v)
 #pragma unroll
       for (int w = 0; w < W; ++w) wv[w][v] = flat[v * W + w];
+  } else if (a.weight.dtype == CC1D_FLOAT32 && a.weight.s1 == 1) {
+    const float* wp = static_cast<const float*>(a.weight.data);
+#pragma unroll
+    for (int v = 0; v < VEC; ++v)
+#pragma unroll
+      for (int w = 0; w < W; ++w) wv[w][v] = d0 + v < a.dim ? __ldg(wp + (d0 + v) * a.weight.s0 + w) : 0.f;
   } else {
 #pragma unroll
     for (int v = 0; v < VEC; ++v)
@@ -62,29 +78,24 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
 #pragma unroll
   for (int v = 0; v < VEC; ++v) bv[v] = a.bias.data ? load_any(a.bias.data, a.bias.dtype, (d0 + v) * a.bias.s0) : 0.f;
 
-  // phase 1: row indices, then every row's history window and first input
-  int64_t row[BR], cache[BR];
-  bool ok[BR];
+  // history windows (circular: positions base-(W-1) .. base-1 mod S; otherwise the last
+  // W-1 entries of the row)
 #pragma unroll
   for (int r = 0; r < BR; ++r) {
-    const int64_t b = b0 + r;
-    ok[r] = b < a.batch;
-    row[r] = (ok[r] && a.indices) ? (int64_t)a.indices[b * a.indices_stride] : b;
-    cache[r] = (ok[r] && a.cache_seqlens) ? (int64_t)a.cache_seqlens[b * a.cache_stride] : 0;
-  }
-  Packet<T, VEC> hist[BR][W - 1], x0[BR];
+    if (!ok[r] || row[r] < 0) continue;
+    if (a.cache_seqlens) {
+      base[r] %= S;
+      if (base[r] < 0) base[r] += S;
+    }
+    const T* sp = static_cast<const T*>(a.state.data) + (int64_t)row[r] * a.state.s0 + d0 * a.state.s1;
 #pragma unroll
-  for (int r = 0; r < BR; ++r) {
-    if (!ok[r]) continue;
-    const T* xp = static_cast<const T*>(a.x.data) + (b0 + r) * a.x.s0 + d0 * a.x.s1;
-    x0[r] = ld_packet<T, VEC>(xp);
-    if (row[r] >= 0) {
-      const T* sp = static_cast<const T*>(a.state.data) + row[r] * a.state.s0 + d0 * a.state.s1;
-#pragma unroll
-      for (int i = 0; i < W - 1; ++i) {
-        const int64_t pos = a.cache_seqlens ? pos_mod(cache[r] - (W - 1) + i, S) : S - (W - 1) + i;
-        hist[r][i] = ld_packet<T, VEC>(sp + pos * a.state.s2);
+    for (int i = 0; i < W - 1; ++i) {
+      int pos = S - (W - 1) + i;
+      if (a.cache_seqlens) {
+        pos = base[r] - (W - 1) + i;  // >= -(W-1) >= -S
+        if (pos < 0) pos += S;
       }
+      hist[r][i] = ld_packet<T, VEC>(sp + (int64_t)pos * a.state.s2);
     }
   }
 
@@ -99,13 +110,13 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
       float z[VEC];
 #pragma unroll
       for (int v = 0; v < VEC; ++v) z[v] = 0.f;
-      for (int64_t t = 0; t < T_len; ++t) st_packet<T, VEC>(op + t * a.out.s2, pack<T, VEC>(z));
+      for (int t = 0; t < T_len; ++t) st_packet<T, VEC>(op + t * a.out.s2, pack<T, VEC>(z));
       continue;
     }
     float hw[W - 1][VEC];
 #pragma unroll
     for (int i = 0; i < W - 1; ++i) unpack<T, VEC>(hist[r][i], hw[i]);
-    for (int64_t t = 0; t < T_len; ++t) {
+    for (int t = 0; t < T_len; ++t) {
       float xc[VEC];
       unpack<T, VEC>(t == 0 ? x0[r] : ld_packet<T, VEC>(xp + t * a.x.s2), xc);
       float acc[VEC];
@@ -133,10 +144,13 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
   for (int r = 0; r < BR; ++r) {
     if (!ok[r] || row[r] < 0) continue;
     const T* xp = static_cast<const T*>(a.x.data) + (b0 + r) * a.x.s0 + d0 * a.x.s1;
-    T* sp = static_cast<T*>(a.state.data) + row[r] * a.state.s0 + d0 * a.state.s1;
+    T* sp = static_cast<T*>(a.state.data) + (int64_t)row[r] * a.state.s0 + d0 * a.state.s1;
     if (a.cache_seqlens) {
-      for (int64_t t = 0; t < T_len; ++t)  // in order: with seqlen > state_len the last write wins
-        st_packet<T, VEC>(sp + pos_mod(cache[r] + t, S) * a.state.s2, t == 0 ? x0[r] : ld_packet<T, VEC>(xp + t * a.x.s2));
+      int pos = base[r];
+      for (int t = 0; t < T_len; ++t) {  // in order: with seqlen > state_len the last write wins
+        st_packet<T, VEC>(sp + (int64_t)pos * a.state.s2, t == 0 ? x0[r] : ld_packet<T, VEC>(xp + t * a.x.s2));
+        pos = pos + 1 == S ? 0 : pos + 1;
+      }
     } else if (S == W - 1 && T_len == 1) {
       // the whole old state is the history window: shift it from registers
 #pragma unroll
@@ -146,17 +160,17 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
       // new[s] = old[s + T] (s + T < S) or x[s + T - S].  Positions move down, so a group
       // of G positions is read completely before it is written, in ascending groups.
       constexpr int G = 4;
-      for (int64_t s0 = 0; s0 < S; s0 += G) {
+      for (int s0 = 0; s0 < S; s0 += G) {
         Packet<T, VEC> v[G];
 #pragma unroll
         for (int q = 0; q < G; ++q) {
-          const int64_t src = s0 + q + T_len;
+          const int src = s0 + q + T_len;
           if (s0 + q < S)
-            v[q] = (src < S) ? ld_packet<T, VEC>(sp + src * a.state.s2) : ld_packet<T, VEC>(xp + (src - S) * a.x.s2);
+            v[q] = (src < S) ? ld_packet<T, VEC>(sp + (int64_t)src * a.state.s2) : ld_packet<T, VEC>(xp + (int64_t)(src - S) * a.x.s2);
         }
 #pragma unroll
         for (int q = 0; q < G; ++q)
-          if (s0 + q < S) st_packet<T, VEC>(sp + (s0 + q) * a.state.s2, v[q]);
+          if (s0 + q < S) st_packet<T, VEC>(sp + (int64_t)(s0 + q) * a.state.s2, v[q]);
       }
     }
   }
