@@ -46,15 +46,35 @@ class GradBucket:
         self.dbias = self.flat[dim * width:] if has_bias else None
 
 
-def allreduce_param_grads(bucket: GradBucket, group=None) -> None:
-    """Sum the bucket over the process group (no-op without an initialised group)."""
-    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+def allreduce_param_grads(bucket: GradBucket, group=None, deterministic: bool = False) -> None:
+    """Sum the bucket over the process group (no-op without an initialised group).
+
+    ``deterministic=True`` gathers every rank's partial sums and adds them locally in
+    rank order, so the result is bit-identical on every rank and from run to run
+    whatever algorithm the collective library picks; the default is one all-reduce.
+    """
+    if not (dist.is_available() and dist.is_initialized()):
+        return
+    world = dist.get_world_size(group)
+    if world <= 1:
+        return
+    if not deterministic:
         dist.all_reduce(bucket.flat, op=dist.ReduceOp.SUM, group=group)
+        return
+    n = bucket.flat.numel()
+    parts = torch.empty(world * n, dtype=bucket.flat.dtype, device=bucket.flat.device)
+    dist.all_gather_into_tensor(parts, bucket.flat, group=group)
+    parts = parts.view(world, n)
+    total = parts[0].clone()
+    for r in range(1, world):
+        total += parts[r]
+    bucket.flat.copy_(total)
 
 
 def causal_conv1d_bwd_batch_sharded(x, weight, bias, dout, seq_idx=None, initial_states=None,
                                     dfinal_states=None, silu_activation=False, return_dinitial_states=False,
-                                    bucket: GradBucket | None = None, group=None, allreduce=True):
+                                    bucket: GradBucket | None = None, group=None, allreduce=True,
+                                    deterministic: bool = False):
     """Backward of this rank's batch shard, then the dweight/dbias all-reduce.
 
     Returns ``(dx, dweight, dbias, dinitial_states)`` like
@@ -72,7 +92,7 @@ def causal_conv1d_bwd_batch_sharded(x, weight, bias, dout, seq_idx=None, initial
     _abi.bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial,
              bucket.dweight, bucket.dbias, silu_activation)
     if allreduce:
-        allreduce_param_grads(bucket, group)
+        allreduce_param_grads(bucket, group, deterministic)
     dw = bucket.dweight if weight.dtype == torch.float32 else bucket.dweight.to(weight.dtype)
     db = None
     if bias is not None:

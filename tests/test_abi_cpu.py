@@ -116,3 +116,26 @@ def test_struct_layout_matches_ctypes(tmp_path):
         "cc1d_varlen_states_params.states": _abi.VarlenParams.states.offset,
     }
     assert {k: int(v) for k, v in got.items()} == py
+
+
+def test_torch_ops_registered_with_fake_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import causal_conv1d  # noqa: F401  (registers the operators)
+    import torch
+
+    for name in ("fwd", "bwd", "update", "varlen_states"):
+        assert hasattr(torch.ops.causal_conv1d, name), name
+    with FakeTensorMode():
+        x = torch.empty(2, 512, 64).transpose(1, 2)  # (batch, dim, seqlen), channel-last
+        w = torch.empty(64, 4)
+        b = torch.empty(64)
+        out = torch.ops.causal_conv1d.fwd(x, w, b, None, None, None, True)
+        assert out.shape == x.shape and out.stride() == x.stride()
+        dx, dw, db, di = torch.ops.causal_conv1d.bwd(x, w, b, x, None, None, None, False, True)
+        assert dx.shape == x.shape and dw.shape == (64, 4) and db.shape == (64,) and di.numel() == 0
+        st = torch.empty(2, 64, 3)
+        assert torch.ops.causal_conv1d.update(x[:, :, :1], st, w, b, True, None, None).shape == (2, 64, 1)
+        xs = torch.empty(100, 64)
+        cu = torch.empty(4, dtype=torch.int32)
+        assert torch.ops.causal_conv1d.varlen_states(xs, cu, 3).shape == (3, 64, 3)

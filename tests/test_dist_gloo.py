@@ -54,6 +54,37 @@ def _sharded_worker(rank, world, port, result_dir):
         dist.destroy_process_group()
 
 
+def _deterministic_worker(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        bucket = GradBucket(8, 4, True, "cpu")
+        bucket.flat.copy_(torch.from_numpy(_rank_partials(world)[rank]))
+        allreduce_param_grads(bucket, deterministic=True)
+        np.save(os.path.join(result_dir, f"rank{rank}.npy"), bucket.flat.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def _rank_partials(world):
+    # magnitudes far apart, so that fp32 sums depend on their order
+    rng = np.random.default_rng(11)
+    n = 8 * 4 + 8
+    return [(rng.standard_normal(n) * 10.0 ** (3 * (r % 3))).astype(np.float32) for r in range(world)]
+
+
+def test_deterministic_reduction_is_rank_ordered(tmp_path):
+    world = 3
+    mp.spawn(_deterministic_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    parts = _rank_partials(world)
+    expected = parts[0].copy()
+    for r in range(1, world):
+        expected = (expected + parts[r]).astype(np.float32)
+    for r in range(world):
+        got = np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))
+        assert np.array_equal(got, expected), r
+
+
 def test_batch_sharded_backward_allreduce(tmp_path):
     world = 2
     mp.spawn(_sharded_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
