@@ -139,3 +139,10 @@ def test_torch_ops_registered_with_fake_shapes():
         xs = torch.empty(100, 64)
         cu = torch.empty(4, dtype=torch.int32)
         assert torch.ops.causal_conv1d.varlen_states(xs, cu, 3).shape == (3, 64, 3)
+
+
+def test_legacy_module_function_table():
+    import causal_conv1d_cuda
+
+    for name in ("causal_conv1d_fwd", "causal_conv1d_bwd", "causal_conv1d_update"):
+        assert callable(getattr(causal_conv1d_cuda, name))
