@@ -343,6 +343,41 @@ __device__ __forceinline__ int64_t part_start(int64_t s, int64_t n, int64_t len)
   return static_cast<int64_t>(us * base + min(us, rem));
 }
 
+// seq_idx of consecutive rows for a warp's walk: 32 rows at a time are fetched with one
+// coalesced load (lane i holds row block + i), one block ahead of use, and each row's
+// value reaches every lane by __shfl_sync - no per-row dependent load.  Rows at or past
+// `end` read as -1.  Every lane of the warp must call next() together.
+struct SeqFeed {
+  const int* p;
+  int64_t stride, pos, end;  // pos: first row of the next block to load
+  int cur, nxt, k;
+  __device__ __forceinline__ int load(int lane) const {
+    const int64_t r = pos + lane;
+    return r < end ? __ldg(p + r * stride) : -1;
+  }
+  __device__ __forceinline__ void start(const int* row0, int64_t s, int64_t first, int64_t end_rows, int lane) {
+    p = row0;
+    stride = s;
+    end = end_rows;
+    pos = first;
+    cur = load(lane);
+    pos += 32;
+    nxt = load(lane);
+    pos += 32;
+    k = 0;
+  }
+  __device__ __forceinline__ int next(int lane) {
+    const int v = __shfl_sync(0xffffffffu, cur, k);
+    if (++k == 32) {
+      k = 0;
+      cur = nxt;
+      nxt = load(lane);
+      pos += 32;
+    }
+    return v;
+  }
+};
+
 // Weight and bias of VEC consecutive channels, as fp32.
 // fp32 (dim, W) weight with unit channel stride and fp32 unit-stride bias (or none) take
 // a branch-free path whose loads all issue back to back.

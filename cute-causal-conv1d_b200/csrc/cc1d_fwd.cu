@@ -185,14 +185,24 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   }
 
   T* optr = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 + l0 * so;
+  // seq_idx: warps whose 32 lanes all hold channels (the others returned above) share
+  // one coalesced load per 32 rows through SeqFeed's shuffles; a warp at the channel
+  // edge, where some lanes have left, reads each row's value directly.
+  const bool full_warp = (pb * 32 + 32) <= a.nv;  // the same for every lane of the warp
+  SeqFeed seq;
   const int* sptr = SEQ ? srow + l0 * a.seq_idx.s1 : nullptr;
+  if (SEQ && full_warp) seq.start(srow, a.seq_idx.s1, l0, L, lane);
   auto row = [&](const Pk& raw) {
     float2 xc[H];
     unpack2<T, VEC>(raw, xc);
     int scur = 0;
     if constexpr (SEQ) {
-      scur = *sptr;
-      sptr += a.seq_idx.s1;
+      if (full_warp) {
+        scur = seq.next(lane);
+      } else {
+        scur = *sptr;
+        sptr += a.seq_idx.s1;
+      }
     }
     float2 acc[H];
 #pragma unroll
