@@ -362,6 +362,7 @@ struct BwdWalk {
 // prefetch and no branches.
 template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT>
 __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
+  grid_dependency_wait();  // launched as a programmatic dependent launch
   using Pk = Packet<T, VEC>;
   constexpr int H = VEC / 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -877,7 +878,8 @@ static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
     const auto kern = bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kBwdStreamThreads>;           \
     const cudaError_t ea = allow_dynamic_smem(reinterpret_cast<const void*>(kern), ls.smem);                   \
     if (ea != cudaSuccess) return ea;                                                                 \
-    kern<<<ls.grid, kBwdStreamThreads, ls.smem, s>>>(a);                                              \
+    const cudaError_t el = launch_dependent(kern, ls.grid, dim3(kBwdStreamThreads), ls.smem, s, a);    \
+    if (el != cudaSuccess) return el;                                                                 \
   }
       if (silu) { if (seq) CC1D_GO(true, true) else CC1D_GO(true, false) }
       else { if (seq) CC1D_GO(false, true) else CC1D_GO(false, false) }

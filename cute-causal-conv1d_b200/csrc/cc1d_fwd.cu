@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(kThreads) fwd_channel_last_kernel(const ConvAr
 // bias are pre-scaled by 1/2 so the accumulator is h = p/2 and silu(p) = h*tanh(h) + h.
 template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT>
 __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
+  grid_dependency_wait();  // launched as a programmatic dependent launch
   using Pk = Packet<T, VEC>;
   constexpr int H = VEC / 2;
   constexpr bool HALF_ARG = SILU && !std::is_same<T, float>::value;
@@ -414,7 +415,8 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 8) {
-#define CC1D_GO(SI, SQ) fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kFwdStreamThreads><<<ls.grid, kFwdStreamThreads, ls.smem, s>>>(a)
+#define CC1D_GO(SI, SQ) \
+  return launch_dependent(fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kFwdStreamThreads>, ls.grid, dim3(kFwdStreamThreads), ls.smem, s, a)
       if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
       else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
 #undef CC1D_GO

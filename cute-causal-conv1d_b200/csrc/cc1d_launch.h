@@ -46,6 +46,26 @@ CC1D_DECLARE(fwd)
 CC1D_DECLARE(bwd)
 #undef CC1D_DECLARE
 
+// Launches `kernel` as a programmatic dependent launch: its CTAs may be scheduled while
+// the previous kernel on the stream retires, and the kernel's first action,
+// grid_dependency_wait(), holds them until that kernel has completed and its writes are
+// visible.  Ordering with any earlier work is therefore the same as a plain launch.
+template <typename Kernel, typename Arg>
+inline cudaError_t launch_dependent(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                    const Arg& arg) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, arg);
+}
+
 // Sets the message returned by cc1d_last_error() on the calling thread.
 void set_last_error(const char* msg);
 
