@@ -182,6 +182,7 @@ struct WalkFeed {
 // STATES: initial_states and/or final_states are given (compiled out otherwise).
 template <typename T, int W, bool SILU, bool STATES, int P, int NT>
 __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
+  grid_dependency_wait();  // launched as a programmatic dependent launch
   constexpr int VEC = 16 / sizeof(T);
   constexpr int H2 = VEC / 2;
   constexpr int S = 32 * VEC;
@@ -291,6 +292,7 @@ __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
 // STATES: initial_states, dinitial_states and/or dfinal_states are given.
 template <typename T, int W, bool SILU, bool STATES, int P, int NT>
 __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
+  grid_dependency_wait();  // launched as a programmatic dependent launch
   constexpr int VEC = 16 / sizeof(T);
   constexpr int H2 = VEC / 2;  // fp32 pairs hold elements (m, m + H2), as in the forward
   constexpr int S = 32 * VEC;
@@ -528,7 +530,8 @@ static cudaError_t launch_rowwalk_w(bool bwd, const ConvArgs& a, const LaunchSha
     const auto kern = K<T, W, SI, ST, kRowWalkDepth, kRowWalkThreads>;                       \
     const cudaError_t ea = allow_dynamic_smem(reinterpret_cast<const void*>(kern), ls.smem); \
     if (ea != cudaSuccess) return ea;                                                        \
-    kern<<<ls.grid, kRowWalkThreads, ls.smem, s>>>(a);                                       \
+    const cudaError_t el = launch_dependent(kern, ls.grid, dim3(kRowWalkThreads), ls.smem, s, a); \
+    if (el != cudaSuccess) return el;                                                        \
   }
   if (!bwd) {
     if (ls.silu) { if (states) CC1D_GO(fwd_rowwalk_kernel, true, true) else CC1D_GO(fwd_rowwalk_kernel, true, false) }

@@ -10,12 +10,14 @@
 // of the last state_len tokens of each packed sequence (zero where the sequence is
 // shorter), bit exact.
 #include "cc1d_common.cuh"
+#include "cc1d_launch.h"
 #include "cc1d_update_launch.h"
 
 namespace cc1d {
 
 template <typename T, int W, int VEC>
 __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
+  grid_dependency_wait();  // launched as a programmatic dependent launch
   // CTA tile: 32 channel packets x (8 warps x BR batch rows).  A thread owns one packet
   // for BR batch rows: it loads the weights once, issues the loads of all BR rows before
   // using any of them (the rows' memory latencies overlap), then computes and writes.
@@ -178,6 +180,7 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
 
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kThreads) varlen_states_kernel(const VarlenArgs a) {
+  grid_dependency_wait();  // launched as a programmatic dependent launch
   const int64_t nv = (a.dim + VEC - 1) / VEC;
   const int64_t total = nv * a.state_len * a.batch;
   for (int64_t item = (int64_t)blockIdx.x * kThreads + threadIdx.x; item < total;
@@ -206,23 +209,25 @@ __global__ void __launch_bounds__(kThreads) varlen_states_kernel(const VarlenArg
 template <typename T>
 static cudaError_t launch_update_t(const UpdateArgs& a, int width, bool packet, dim3 grid, cudaStream_t s) {
   constexpr int PV = 8 / sizeof(T);  // 8-byte packets: more threads, fewer registers per thread
+  cudaError_t e;
   switch (width * 2 + (packet ? 1 : 0)) {
-    case 4: update_kernel<T, 2, 1><<<grid, kThreads, 0, s>>>(a); break;
-    case 5: update_kernel<T, 2, PV><<<grid, kThreads, 0, s>>>(a); break;
-    case 6: update_kernel<T, 3, 1><<<grid, kThreads, 0, s>>>(a); break;
-    case 7: update_kernel<T, 3, PV><<<grid, kThreads, 0, s>>>(a); break;
-    case 8: update_kernel<T, 4, 1><<<grid, kThreads, 0, s>>>(a); break;
-    case 9: update_kernel<T, 4, PV><<<grid, kThreads, 0, s>>>(a); break;
+    case 4: e = launch_dependent(update_kernel<T, 2, 1>, grid, dim3(kThreads), 0, s, a); break;
+    case 5: e = launch_dependent(update_kernel<T, 2, PV>, grid, dim3(kThreads), 0, s, a); break;
+    case 6: e = launch_dependent(update_kernel<T, 3, 1>, grid, dim3(kThreads), 0, s, a); break;
+    case 7: e = launch_dependent(update_kernel<T, 3, PV>, grid, dim3(kThreads), 0, s, a); break;
+    case 8: e = launch_dependent(update_kernel<T, 4, 1>, grid, dim3(kThreads), 0, s, a); break;
+    case 9: e = launch_dependent(update_kernel<T, 4, PV>, grid, dim3(kThreads), 0, s, a); break;
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+  return e;
 }
 
 template <typename T>
 static cudaError_t launch_varlen_t(const VarlenArgs& a, bool packet, dim3 grid, cudaStream_t s) {
   constexpr int PV = 16 / sizeof(T);
-  if (packet) varlen_states_kernel<T, PV><<<grid, kThreads, 0, s>>>(a);
-  else varlen_states_kernel<T, 1><<<grid, kThreads, 0, s>>>(a);
+  const cudaError_t e = packet ? launch_dependent(varlen_states_kernel<T, PV>, grid, dim3(kThreads), 0, s, a)
+                               : launch_dependent(varlen_states_kernel<T, 1>, grid, dim3(kThreads), 0, s, a);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
