@@ -12,9 +12,9 @@ dweight|dbias are summed with one NCCL all-reduce per step.
 
 Inputs rotate over 4 buffer sets (1 GiB in total, > 8x the 126 MB L2); the forward of
 step i reads set i % 4 and the backward reads set (i + 2) % 4, so no kernel reads data
-another kernel touched within the previous ~300 MB of traffic.  On one GPU the timed
-loop replays one CUDA graph per 4 steps; per-kernel times come from a graph of 16
-back-to-back launches of each pass.
+another kernel touched within the previous ~300 MB of traffic.  The timed loop replays
+one CUDA graph per 16 steps; per-kernel times come from a graph of 16 back-to-back
+launches of each pass.
 
 `--impl reference` times the reference algorithm's CPU implementation (the C
 restatement in oracle/, OpenMP on all host cores) on a bounded sample of the same
@@ -39,6 +39,7 @@ for _p in (ROOT, os.path.join(ROOT, "cute-causal-conv1d_b200")):
 METRIC = "fwd/bwd/update achieved HBM GB/s and % of 8 TB/s roofline at 1/2/4/8 B200"
 CFG2 = dict(batch=4, dim=4096, seqlen=2048, width=4)
 NSETS = 4
+GRAPH_STEPS = 4 * NSETS  # steps per replay of the timed step graph
 
 
 def workload_bytes(batch, dim, seqlen, width, es=2, init=True, final=True, bias=True):
@@ -249,6 +250,9 @@ def run_ours(args):
     if world > 1:
         import datetime
 
+        # the per-step all-reduce moves 80 KB: NVLink SHARP brings nothing at that size,
+        # so it stays off (no multicast memory objects are created)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     _abi.load_library()
 
@@ -302,25 +306,30 @@ def run_ours(args):
         if world > 1:
             allreduce_param_grads(sets[kb]["bucket"])
 
-    # One graph holds NSETS consecutive steps, so that no graph-launch gap sits between
-    # the kernels of the timed steps.  With N ranks each step's dweight|dbias all-reduce
-    # is captured on a side stream: it overlaps the next step's forward, and the graph
-    # joins it before it ends.
+    # One graph holds GRAPH_STEPS consecutive steps, so that no graph-launch gap sits
+    # between the kernels of the timed steps.  With N ranks each step's dweight|dbias
+    # all-reduce is captured on a side stream, overlapping the next steps; the backward
+    # that rewrites a bucket waits for the all-reduce that read it, and the graph joins
+    # the side stream before it ends.
     side = torch.cuda.Stream(dev) if world > 1 else None
     if side is not None:
         allreduce_param_grads(sets[0]["bucket"])  # communicator set up before capture
         torch.cuda.synchronize()
     g_round = torch.cuda.CUDAGraph()
+    reduced = [torch.cuda.Event() for _ in range(NSETS)]  # all-reduce of set k's bucket done
     with torch.cuda.graph(g_round):
         cap = torch.cuda.current_stream()
-        for i in range(NSETS):
+        for i in range(GRAPH_STEPS):
             fwd(i % NSETS)
             kb = (i + NSETS // 2) % NSETS
+            if side is not None and i >= NSETS:
+                cap.wait_event(reduced[kb])  # the all-reduce that read this bucket, NSETS steps ago
             bwd(kb)
             if side is not None:
                 side.wait_stream(cap)
                 with torch.cuda.stream(side):
                     allreduce_param_grads(sets[kb]["bucket"])
+                    reduced[kb].record(side)
         if side is not None:
             cap.wait_stream(side)
     torch.cuda.synchronize()
@@ -328,9 +337,9 @@ def run_ours(args):
     def run_steps(n):
         i = 0
         if g_round is not None:
-            while i + NSETS <= n:
+            while i + GRAPH_STEPS <= n:
                 g_round.replay()
-                i += NSETS
+                i += GRAPH_STEPS
         while i < n:
             step(i)
             i += 1
