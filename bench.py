@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-Workload: bf16 x (4, 4096, 2048) channel-last, fp32 weight (4096, 4)
+Workload (benchmark config 2): bf16 x (4, 4096, 2048) channel-last, fp32 weight (4096, 4)
 ~U(-0.5, 0.5) and bias ~N(0, 0.1), SiLU, initial_states (4, 4096, 3), final states
 returned; one step = forward + backward (dx, dweight, dbias, dinitial_states, dfinal fed
 back).  Metric: algorithmic HBM GB/s (every tensor element read or written once).  Each
@@ -529,7 +529,7 @@ def graph_time(fns, reps=5):
 
 
 def run_extras(dev):
-    """Kernel-level numbers for the other BASELINE configs (outside the timed step)."""
+    """Kernel-level numbers for the other benchmark configs (outside the timed step)."""
     import torch
 
     from causal_conv1d import causal_conv1d_update

@@ -264,7 +264,7 @@ def gen_varlen(w: Writer):
 
 
 def gen_config1(w: Writer):
-    """fp32 (2, 64, 512) contiguous, W=4, silu, seed 0."""
+    """Benchmark config 1: fp32 (2, 64, 512) contiguous, W=4, silu, seed 0."""
     gen = torch.Generator().manual_seed(0)
     x = torch.randn(2, 64, 512, generator=gen)
     weight = torch.rand(64, 4, generator=gen) - 0.5

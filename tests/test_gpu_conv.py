@@ -286,7 +286,7 @@ def test_mixed_layout_dout():
 
 
 def test_fwd_function_final_states_contiguous_buffer():
-    """final_states_out may be (batch, dim, width-1) contiguous (BASELINE layout)."""
+    """final_states_out may be (batch, dim, width-1) contiguous (the benchmark's layout)."""
     gen = torch.Generator().manual_seed(4)
     x = torch.randn(4, 256, 37, generator=gen).to(torch.bfloat16)
     w = torch.randn(256, 4, generator=gen) - 0.5

@@ -1,6 +1,6 @@
 """Tolerances used by the parity tests.
 
-Kernel vs oracle (the parity bar): the north-star table, taking the reference test's
+Kernel vs oracle (the parity bar): the benchmark's tolerance table, taking the reference test's
 stricter bf16 pair (``tests/test_causal_conv1d.py:75-78`` in the reference):
 fp32 3e-4/1e-3, fp16 3e-3/5e-3, bf16 1e-2/5e-2; dweight/dbias 1e-3/1e-3 for fp32
 parameters, and 1e-2/5e-2 for 16-bit parameters (reference
