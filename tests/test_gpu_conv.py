@@ -298,3 +298,30 @@ def test_fwd_function_final_states_contiguous_buffer():
                    silu=True, return_final_states=True)
     assert_close(out, eo, "bfloat16", PARITY["bfloat16"])
     assert np.array_equal(to_storage(fin), ef)
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+@pytest.mark.parametrize("seqlen", [8, 96, 256, 1000])
+@pytest.mark.parametrize("width", [2, 4])
+def test_contiguous_states_through_functions(dt, seqlen, width):
+    """(batch, dim, seqlen)-contiguous x with initial/final states and dinitial/dfinal.
+    The public interface only returns final states for channel-last x, so this drives
+    the row-walk state handling through the host functions directly."""
+    from causal_conv1d.cpp_functions import causal_conv1d_bwd_function, causal_conv1d_fwd_function
+
+    gen = torch.Generator().manual_seed(seqlen * 17 + width)
+    x, w, b, init, dout, dfinal = make_inputs(gen, 3, 40, seqlen, width, dt, True, True, True)
+    fin = torch.empty(3, 40, width - 1, dtype=TORCH_DT[dt], device="cuda")
+    out = causal_conv1d_fwd_function(x.cuda(), w.cuda(), b.cuda(), None, init.cuda(), fin, True)
+    dx, dw, db, di = causal_conv1d_bwd_function(x.cuda(), w.cuda(), b.cuda(), dout.cuda(), None, init.cuda(),
+                                                dfinal.cuda(), None, True, True)
+    xs, ws, bs, inits = to_storage(x), to_storage(w), to_storage(b), to_storage(init)
+    eo, ef = O.fwd(xs, dt, ws, "float32", bs, "float32", initial_states=inits, silu=True, return_final_states=True)
+    edx, edw, edb, edi = O.bwd(xs, dt, ws, "float32", to_storage(dout), bs, "float32", initial_states=inits,
+                               dfinal_states=to_storage(dfinal), silu=True)
+    assert_close(out, eo, dt, PARITY[dt], "out")
+    assert np.array_equal(to_storage(fin), ef)
+    assert_close(dx, edx, dt, PARITY[dt], "dx")
+    assert_close(dw, edw, "float32", GRAD_PARAM["float32"], "dweight")
+    assert_close(db, edb, "float32", GRAD_PARAM["float32"], "dbias")
+    assert_close(di, edi, dt, PARITY[dt], "dinitial")
