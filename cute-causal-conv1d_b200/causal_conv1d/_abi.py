@@ -68,6 +68,13 @@ class VarlenParams(ctypes.Structure):
     ]
 
 
+class FwdVarlenStatesParams(ctypes.Structure):
+    _fields_ = [
+        ("fwd", FwdParams), ("nseq", c_i64), ("state_len", c_i64),
+        ("cu_seqlens", CTensor), ("states", CTensor),
+    ]
+
+
 # Bytes of the library's static backward scratch array (CC1D_STATIC_SCRATCH_BYTES).
 STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
 
@@ -79,6 +86,7 @@ SIGNATURES = {
     "cc1d_bwd_launch_static": (c_i32, [ctypes.POINTER(BwdParams), c_void_p]),
     "cc1d_update_launch": (c_i32, [ctypes.POINTER(UpdateParams), c_void_p]),
     "cc1d_varlen_states_launch": (c_i32, [ctypes.POINTER(VarlenParams), c_void_p]),
+    "cc1d_fwd_varlen_states_launch": (c_i32, [ctypes.POINTER(FwdVarlenStatesParams), c_void_p]),
     "cc1d_last_error": (ctypes.c_char_p, []),
     "cc1d_status_string": (ctypes.c_char_p, [c_i32]),
     "cc1d_abi_version": (c_i32, []),
@@ -220,6 +228,18 @@ def varlen_states(x, cu_seqlens, states) -> None:
                      _ct(x), _ct(cu_seqlens), _ct(states))
     with _Guard(dev) as stream:
         _check(lib.cc1d_varlen_states_launch(ctypes.byref(p), stream))
+
+
+def fwd_varlen_states(x, weight, bias, seq_idx, cu_seqlens, states, out, silu: bool) -> None:
+    lib = load_library()
+    dev = _device_of(x, weight, bias, seq_idx, cu_seqlens, states, out)
+    f = FwdParams(
+        x.shape[0], x.shape[1], x.shape[2], weight.shape[1],
+        _ct(x), _ct(weight), _ct(bias), _ct(seq_idx), _ct(None), _ct(None), _ct(out), int(bool(silu)), 0,
+    )
+    p = FwdVarlenStatesParams(f, states.shape[0], states.shape[2], _ct(cu_seqlens), _ct(states))
+    with _Guard(dev) as stream:
+        _check(lib.cc1d_fwd_varlen_states_launch(ctypes.byref(p), stream))
 
 
 def launch_count() -> int:

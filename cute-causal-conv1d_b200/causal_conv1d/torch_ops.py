@@ -1,4 +1,5 @@
-"""PyTorch operator registrations: ``torch.ops.causal_conv1d.{fwd,bwd,update,varlen_states}``.
+"""PyTorch operator registrations:
+``torch.ops.causal_conv1d.{fwd,bwd,update,varlen_states,fwd_varlen_states}``.
 
 The same launches as :mod:`causal_conv1d.cpp_functions`, registered as custom operators
 with their mutated arguments declared (``final_states_out`` of ``fwd``, ``conv_state`` of
@@ -13,6 +14,7 @@ them.
   when there is no bias or no initial-state gradient.
 * ``update(x, conv_state, weight, bias, silu, cache_seqlens, conv_state_indices) -> out``
 * ``varlen_states(x, cu_seqlens, state_len) -> states``
+* ``fwd_varlen_states(x, weight, bias, seq_idx, cu_seqlens, state_len, silu) -> (out, states)``
 
 The reference compiles its kernels with the CuTe DSL and registers no torch operators;
 these registrations are this package's equivalent of the C++ extension's op table.
@@ -24,6 +26,7 @@ import torch
 from torch import Tensor
 
 from causal_conv1d import cpp_functions as _cf
+from causal_conv1d.causal_conv1d_varlen import causal_conv1d_fn_varlen_states as _fwd_varlen_states
 from causal_conv1d.causal_conv1d_varlen import causal_conv1d_varlen_states as _varlen_states
 
 _EMPTY = (0,)
@@ -86,3 +89,16 @@ def varlen_states(x: Tensor, cu_seqlens: Tensor, state_len: int) -> Tensor:
 def _(x, cu_seqlens, state_len):
     batch = cu_seqlens.shape[0] - 1
     return x.new_empty(batch, state_len, x.shape[1]).transpose(1, 2)
+
+
+@torch.library.custom_op("causal_conv1d::fwd_varlen_states", mutates_args=())
+def fwd_varlen_states(x: Tensor, weight: Tensor, bias: Tensor | None, seq_idx: Tensor | None,
+                      cu_seqlens: Tensor, state_len: int, silu: bool) -> tuple[Tensor, Tensor]:
+    return _fwd_varlen_states(x, weight, cu_seqlens, state_len, bias, seq_idx, "silu" if silu else None)
+
+
+@fwd_varlen_states.register_fake
+def _(x, weight, bias, seq_idx, cu_seqlens, state_len, silu):
+    nseq = cu_seqlens.shape[0] - 1
+    out = torch.empty_like(x) if (x.stride(2) == 1 or x.stride(1) == 1) else torch.empty_like(x.contiguous())
+    return out, x.new_empty(nseq, state_len, x.shape[1]).transpose(1, 2)

@@ -394,9 +394,10 @@ int cc1d_abi_version(void) { return CC1D_ABI_VERSION; }
 
 int64_t cc1d_launch_count(void) { return g_launches.load(); }
 
-cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
-  g_last_error.clear();
-  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+// Validates a forward and plans its launch.  *empty is set when there is nothing to
+// launch (no rows, no channels, or seqlen 0 without final states).
+static cc1d_status fwd_prepare(const cc1d_fwd_params* p, Geometry* out_g, bool* empty) {
+  *empty = true;
   cc1d_status st = check_conv_common(p->batch, p->dim, p->seqlen, p->width, p->x, p->weight, p->bias,
                                      p->seq_idx, p->initial_states);
   if (st != CC1D_OK) return st;
@@ -411,11 +412,12 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
     return CC1D_OK;
   }
   if (!p->out.data) return fail(CC1D_ERR_VALUE, "out is required");
+  *empty = false;
 
   int layout = kLayoutChannelLast;
   bool packet = false;
   const int es = elem_size(p->x.dtype);
-  Geometry g;
+  Geometry& g = *out_g;
   if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->out, B, D, L, 8)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
@@ -456,10 +458,24 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, g.ls), g.ls.smem) * sm_count();
     g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
   }
-  cudaError_t e = dispatch(false, p->x.dtype, a, g.ls, static_cast<cudaStream_t>(stream));
+  return CC1D_OK;
+}
+
+static cc1d_status fwd_run(const cc1d_fwd_params* p, const Geometry& g, void* stream) {
+  cudaError_t e = dispatch(false, p->x.dtype, g.a, g.ls, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d forward launch");
   g_launches.fetch_add(1);
   return CC1D_OK;
+}
+
+cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
+  g_last_error.clear();
+  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+  Geometry g;
+  bool empty = true;
+  const cc1d_status st = fwd_prepare(p, &g, &empty);
+  if (st != CC1D_OK || empty) return st;
+  return fwd_run(p, g, stream);
 }
 
 static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* empty) {
@@ -647,9 +663,9 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   return CC1D_OK;
 }
 
-cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* p, void* stream) {
-  g_last_error.clear();
-  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+// Validates a varlen-states gather; *empty is set when there is nothing to write.
+static cc1d_status varlen_check(const cc1d_varlen_states_params* p, bool* empty) {
+  *empty = true;
   const int64_t B = p->batch, D = p->dim, S = p->state_len;
   if (B < 0 || D < 0 || S < 0 || p->total_tokens < 0) return fail(CC1D_ERR_VALUE, "sizes must be >= 0");
   if (!is_float(p->x.dtype)) return fail(CC1D_ERR_TYPE, "x must be float32, float16, or bfloat16");
@@ -659,6 +675,12 @@ cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* p, void* 
   if (B == 0 || D == 0 || S == 0) return CC1D_OK;
   if (!p->x.data || !p->cu_seqlens.data || !p->states.data)
     return fail(CC1D_ERR_VALUE, "x, cu_seqlens and states are required");
+  *empty = false;
+  return CC1D_OK;
+}
+
+static cc1d_status varlen_run(const cc1d_varlen_states_params* p, void* stream) {
+  const int64_t B = p->batch, D = p->dim, S = p->state_len;
   const int vec = 16 / elem_size(p->x.dtype);
   const bool packet = D % vec == 0 && p->x.stride[1] == 1 && p->states.stride[1] == 1 && aligned16(p->x.data) &&
                       aligned16(p->states.data) && stride_ok(p->x.stride[0], p->total_tokens, vec) &&
@@ -679,6 +701,63 @@ cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* p, void* 
                                        static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d varlen states launch");
   g_launches.fetch_add(1);
+  return CC1D_OK;
+}
+
+cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* p, void* stream) {
+  g_last_error.clear();
+  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+  bool empty = true;
+  const cc1d_status st = varlen_check(p, &empty);
+  if (st != CC1D_OK || empty) return st;
+  return varlen_run(p, stream);
+}
+
+cc1d_status cc1d_fwd_varlen_states_launch(const cc1d_fwd_varlen_states_params* p, void* stream) {
+  g_last_error.clear();
+  if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
+  const cc1d_fwd_params& f = p->fwd;
+  if (f.batch != 1) return fail(CC1D_ERR_VALUE, "packed sequences need batch == 1 (got %lld)", (long long)f.batch);
+  // the gather the forward stands in for: x[0] viewed as (total_tokens = seqlen, dim)
+  cc1d_varlen_states_params v;
+  std::memset(&v, 0, sizeof(v));
+  v.batch = p->nseq;
+  v.dim = f.dim;
+  v.state_len = p->state_len;
+  v.total_tokens = f.seqlen;
+  v.x = f.x;
+  v.x.stride[0] = f.x.stride[2];
+  v.x.stride[1] = f.x.stride[1];
+  v.x.stride[2] = 0;
+  v.cu_seqlens = p->cu_seqlens;
+  v.states = p->states;
+  bool no_states = true, no_fwd = true;
+  cc1d_status st = varlen_check(&v, &no_states);
+  if (st != CC1D_OK) return st;
+  Geometry g;
+  st = fwd_prepare(&f, &g, &no_fwd);
+  if (st != CC1D_OK) return st;
+  // The streamed forward writes the states itself when it runs the packed (seq_idx)
+  // variant, the sequence positions fit its 32-bit row counters and the states take
+  // its 8-byte packets; otherwise the gather runs as its own launch after the forward.
+  const int vec = 8 / elem_size(f.x.dtype);
+  const bool fused = !no_fwd && !no_states && g.ls.layout == kLayoutStream && f.seq_idx.data &&
+                     p->nseq <= kMax32 && p->state_len <= kMax32 && p->states.stride[1] == 1 &&
+                     (reinterpret_cast<uintptr_t>(p->states.data) & 7u) == 0 &&
+                     stride_ok(p->states.stride[0], p->nseq, vec) && stride_ok(p->states.stride[2], p->state_len, vec);
+  if (fused) {
+    ConvArgs& a = g.a;
+    a.states = tensor_arg(p->states);
+    a.cu = p->cu_seqlens.data;
+    a.cu_stride = p->cu_seqlens.stride[0];
+    a.cu_is_64 = p->cu_seqlens.dtype == CC1D_INT64;
+    a.nseq = (int)p->nseq;
+    a.state_len = (int)p->state_len;
+    g.ls.emit = true;
+    return fwd_run(&f, g, stream);
+  }
+  if (!no_fwd && (st = fwd_run(&f, g, stream)) != CC1D_OK) return st;
+  if (!no_states) return varlen_run(&v, stream);
   return CC1D_OK;
 }
 

@@ -301,6 +301,12 @@ struct ConvArgs {
   // columns < seg_r are cut into seg_q + 1 sequence segments, the others into seg_q;
   // unit u is one (column, segment).  The units of one packet block are contiguous.
   int64_t ncol, seg_q, seg_r, units;
+  // forward of packed sequences that also writes their varlen states (batch == 1):
+  // states (nseq, dim, state_len) in x's dtype, cu_seqlens (nseq + 1,) int32 or int64
+  TensorArg states;
+  const void* cu;
+  int64_t cu_stride;
+  int cu_is_64, nseq, state_len;
 };
 
 // First warp unit of column c (c == ncol gives the total).

@@ -15,6 +15,8 @@
 //
 // Both kernels are persistent: the grid is sized to the resident CTA count and each
 // CTA strides over tiles.  Compiled once per element type (CC1D_DT).
+#include <climits>
+
 #include "cc1d_common.cuh"
 #include "cc1d_launch.h"
 
@@ -130,7 +132,140 @@ __global__ void __launch_bounds__(kThreads) fwd_channel_last_kernel(const ConvAr
 // (compile-time ring slots, window rotation by register renaming) and has no bounds
 // checks; arithmetic runs on fp32 pairs (FFMA2).  With 16-bit SiLU the weights and
 // bias are pre-scaled by 1/2 so the accumulator is h = p/2 and silu(p) = h*tanh(h) + h.
-template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT>
+// Varlen decode states written by the streamed forward (EMIT).  The packed rows of
+// sequence k are [cu[k], cu[k+1]); its state slot s holds x row cu[k+1] - S + s when
+// that row is >= cu[k], else zero (the contract of varlen_states_kernel).  Each warp
+// unit stores the slots of the rows it owns, from the packets it streams:
+//  * the zero slots of a sequence shorter than S are written by the unit owning its
+//    first row, when that unit makes the sequence current;
+//  * an empty sequence is zero-filled by the unit owning the last row of the nearest
+//    non-empty sequence before it, or, when there is none, by the unit holding row 0.
+// Every field is the same for all lanes of the warp, so the tests are uniform; cu is
+// read once per sequence (the next end is prefetched when a sequence becomes current).
+// Writes stay inside states for any cu values: k < nseq and 0 <= slot < S always.
+__device__ __forceinline__ int cu_row(const ConvArgs& a, int i) {
+  const int64_t v = a.cu_is_64 ? __ldg(static_cast<const long long*>(a.cu) + i * a.cu_stride)
+                               : static_cast<int64_t>(__ldg(static_cast<const int*>(a.cu) + i * a.cu_stride));
+  return static_cast<int>(min(max(v, int64_t(-1)), a.seqlen + 1));
+}
+
+template <typename T, int VEC>
+struct StateEmitter {
+  T* chan;       // states + d0 (this lane's channel packet)
+  int l0, l1;    // rows of this unit
+  int k;         // current sequence
+  int lo, hi;    // rows [lo, hi) of sequence k have a slot; lo == INT_MAX when done
+  int next_end;  // cu[k + 2] (prefetched), or -2 past the last sequence
+  int pre, pre0; // with nseq <= live lanes: cu[lane + 1] (cu[nseq] past the end) and cu[0]
+
+  __device__ __forceinline__ T* slot(const ConvArgs& a, int kk, int s) const {
+    return chan + kk * a.states.s0 + s * a.states.s2;
+  }
+  __device__ __forceinline__ void zero(const ConvArgs& a, int kk, int n) const {
+    Packet<T, VEC> z;
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) z.v[v] = from_f32<T>(0.f);
+    for (int s = 0; s < n; ++s) st_packet<T, VEC>(slot(a, kk, s), z);
+  }
+  // Makes sequence kk (starting at row c0, ending at c1 when c1 >= -1 is given) or the
+  // next non-empty one current; with `fill`, empty sequences passed over are zeroed.
+  __device__ __forceinline__ void arm(const ConvArgs& a, int kk, int c0, int c1, bool fill) {
+    for (; kk < a.nseq; ++kk) {
+      if (c1 < -1) c1 = cu_row(a, kk + 1);
+      if (c1 > c0) {
+        k = kk;
+        hi = c1;
+        lo = max(c0, c1 - a.state_len);
+        next_end = kk + 1 < a.nseq ? cu_row(a, kk + 2) : -2;
+        if (c1 - c0 < a.state_len && c0 >= l0 && c0 < l1) zero(a, kk, a.state_len - (c1 - c0));
+        return;
+      }
+      if (fill) zero(a, kk, a.state_len);
+      c0 = c1;
+      c1 = -2;
+    }
+    k = a.nseq;
+    lo = hi = INT_MAX;
+  }
+
+  // Issued first in the kernel, before the row prefetch, so that the offsets have
+  // arrived when start() needs them: with at most one sequence per live lane, lane j
+  // loads cu[j + 1] and every lane cu[0].
+  __device__ __forceinline__ void issue(const ConvArgs& a, int lane, int live) {
+    if (a.nseq <= live) {
+      pre = cu_row(a, min(lane, a.nseq - 1) + 1);
+      pre0 = cu_row(a, 0);
+    }
+  }
+
+  // The first sequence ending after row l0 becomes current.  Lanes 0 .. live-1 of the
+  // warp take part (the others have left).  With nseq <= live the offsets loaded by
+  // issue() give it with one ballot and two shuffles; otherwise, with 4 or more lanes,
+  // each round probes `live` candidates at once and narrows the range by that factor,
+  // else a binary search.
+  __device__ __forceinline__ void start(const ConvArgs& a, int64_t d0, int first_row, int end_row, int lane,
+                                        int live) {
+    chan = static_cast<T*>(a.states.data) + d0 * a.states.s1;
+    l0 = first_row;
+    l1 = end_row;
+    const unsigned mask = live >= 32 ? 0xffffffffu : (1u << live) - 1u;
+    const bool row0 = l0 == 0;
+    if (a.nseq <= live) {
+      const unsigned hit = __ballot_sync(mask, pre > l0);  // lanes past nseq repeat cu[nseq]
+      const int k0 = hit ? __ffs(hit) - 1 : a.nseq;
+      const int c1 = __shfl_sync(mask, pre, min(k0, a.nseq - 1));
+      const int c0 = __shfl_sync(mask, pre, max(k0 - 1, 0));
+      if (row0)  // sequences ending at or before row 0 are empty and have no earlier owner
+        for (int j = 0; j < k0; ++j) zero(a, j, a.state_len);
+      arm(a, k0, k0 > 0 ? c0 : pre0, c1, row0);
+      return;
+    }
+    int lo_k = 0, hi_k = a.nseq;  // the answer, first k with cu[k + 1] > l0 or nseq, is in [lo_k, hi_k]
+    if (live >= 4) {
+      while (lo_k < hi_k) {
+        const int step = (hi_k - lo_k + live - 1) / live;
+        const int c = min(lo_k + (lane + 1) * step, hi_k) - 1;  // last candidate of bucket `lane`
+        const unsigned hit = __ballot_sync(mask, cu_row(a, c + 1) > l0);
+        if (hit == 0) {
+          lo_k = hi_k;
+          break;
+        }
+        const int j = __ffs(hit) - 1;
+        hi_k = min(lo_k + (j + 1) * step, hi_k) - 1;
+        lo_k += j * step;
+      }
+    } else {
+      while (lo_k < hi_k) {
+        const int mid = (lo_k + hi_k) >> 1;
+        if (cu_row(a, mid + 1) > l0) hi_k = mid; else lo_k = mid + 1;
+      }
+    }
+    if (row0)
+      for (int j = 0; j < lo_k; ++j) zero(a, j, a.state_len);
+    arm(a, lo_k, lo_k < a.nseq ? cu_row(a, lo_k) : 0, -2, row0);
+  }
+  // Stores row l (streamed as `raw`) if it is a state row of the current sequence.
+  __device__ __forceinline__ void store(const ConvArgs& a, int l, const Packet<T, VEC>& raw) const {
+    if (l >= lo && l < hi) st_packet<T, VEC>(slot(a, k, l - (hi - a.state_len)), raw);
+  }
+  // Row-by-row form: stores row l and moves on after the current sequence's last row.
+  __device__ __forceinline__ void row(const ConvArgs& a, int l, const Packet<T, VEC>& raw) {
+    if (l < lo) return;
+    store(a, l, raw);
+    if (l == hi - 1) arm(a, k + 1, hi, next_end, true);
+  }
+  // Whether a block of rows ending at b1 (and starting at or after the rows already
+  // passed) holds state rows of the current sequence only, so that it can store them
+  // with store() and call after_block() once at its end.
+  __device__ __forceinline__ bool one_sequence(const ConvArgs& a, int b1) const {
+    return b1 < hi || next_end == -2 || next_end - a.state_len >= b1;
+  }
+  __device__ __forceinline__ void after_block(const ConvArgs& a, int b1) {
+    if (b1 >= hi) arm(a, k + 1, hi, next_end, true);
+  }
+};
+
+template <typename T, int W, int VEC, bool SILU, bool SEQ, int P, int NT, bool EMIT = false>
 __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   grid_dependency_wait();  // launched as a programmatic dependent launch
   using Pk = Packet<T, VEC>;
@@ -153,6 +288,9 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   const int64_t d0 = cv * VEC;
   const int64_t sx = a.x.s2, so = a.out.s2;
   const T* xsrc = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 + l0 * sx;
+  [[maybe_unused]] StateEmitter<T, VEC> emit;
+  [[maybe_unused]] const int live = static_cast<int>(min(a.nv - pb * 32, int64_t(32)));  // lanes left in the warp
+  if constexpr (EMIT) emit.issue(a, lane, live);
 
   // prefetch rows l0 .. l0+P-2 before anything else (rows past the segment: zero fill)
 #pragma unroll
@@ -193,6 +331,7 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
   SeqFeed seq;
   const int* sptr = SEQ ? srow + l0 * a.seq_idx.s1 : nullptr;
   if (SEQ && full_warp) seq.start(srow, a.seq_idx.s1, l0, L, lane);
+  if constexpr (EMIT) emit.start(a, d0, static_cast<int>(l0), static_cast<int>(l1), lane, live);
   auto row = [&](const Pk& raw) {
     float2 xc[H];
     unpack2<T, VEC>(raw, xc);
@@ -232,24 +371,76 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
     for (int i = 0; i < H; ++i) xw[W - 2][i] = xc[i];
     sw[W - 2] = scur;
   };
-  // full blocks of P rows: compile-time ring slots, predicated prefetch, no branches
   int j0 = 0;
-  for (; j0 + P <= n; j0 += P) {
+  if constexpr (EMIT) {
+    // The plain loop below, written out again (the same text keeps the same code), up
+    // to the next block holding state rows.  Such a block stores them from the ring;
+    // the rare block that also reaches into the next sequence's state rows goes row
+    // by row.
+    for (;;) {
+      const int64_t plain_end = min(static_cast<int64_t>(n), static_cast<int64_t>(emit.lo) - l0);
+      for (; j0 + P <= plain_end; j0 += P) {
 #pragma unroll
-    for (int u = 0; u < P; ++u) {
-      cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
+        for (int u = 0; u < P; ++u) {
+          cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
+          xsrc += sx;
+          cp_async_commit();
+          cp_async_wait<P - 1>();
+          row(ring[u * NT]);
+        }
+      }
+      if (j0 + P > n) break;
+      const int b1 = static_cast<int>(l0) + j0 + P;
+      if (emit.one_sequence(a, b1)) {
+#pragma unroll
+        for (int u = 0; u < P; ++u) {
+          cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
+          xsrc += sx;
+          cp_async_commit();
+          cp_async_wait<P - 1>();
+          emit.store(a, static_cast<int>(l0) + j0 + u, ring[u * NT]);
+          row(ring[u * NT]);
+        }
+        emit.after_block(a, b1);
+        j0 += P;
+      } else {
+        for (const int j1 = j0 + P; j0 < j1; ++j0) {
+          cp_async_packet<sizeof(Pk)>(ring + ((j0 + P - 1) % P) * NT, xsrc, j0 + P - 1 < n);
+          xsrc += sx;
+          cp_async_commit();
+          cp_async_wait<P - 1>();
+          emit.row(a, static_cast<int>(l0) + j0, ring[(j0 % P) * NT]);
+          row(ring[(j0 % P) * NT]);
+        }
+      }
+    }
+    for (int j = j0; j < n; ++j) {  // remainder
+      cp_async_packet<sizeof(Pk)>(ring + ((j + P - 1) % P) * NT, xsrc, j + P - 1 < n);
       xsrc += sx;
       cp_async_commit();
       cp_async_wait<P - 1>();
-      row(ring[u * NT]);
+      emit.row(a, static_cast<int>(l0) + j, ring[(j % P) * NT]);
+      row(ring[(j % P) * NT]);
     }
-  }
-  for (int j = j0; j < n; ++j) {  // remainder
-    cp_async_packet<sizeof(Pk)>(ring + ((j + P - 1) % P) * NT, xsrc, j + P - 1 < n);
-    xsrc += sx;
-    cp_async_commit();
-    cp_async_wait<P - 1>();
-    row(ring[(j % P) * NT]);
+  } else {
+    // full blocks of P rows: compile-time ring slots, predicated prefetch, no branches
+    for (; j0 + P <= n; j0 += P) {
+#pragma unroll
+      for (int u = 0; u < P; ++u) {
+        cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
+        xsrc += sx;
+        cp_async_commit();
+        cp_async_wait<P - 1>();
+        row(ring[u * NT]);
+      }
+    }
+    for (int j = j0; j < n; ++j) {  // remainder
+      cp_async_packet<sizeof(Pk)>(ring + ((j + P - 1) % P) * NT, xsrc, j + P - 1 < n);
+      xsrc += sx;
+      cp_async_commit();
+      cp_async_wait<P - 1>();
+      row(ring[(j % P) * NT]);
+    }
   }
   cp_async_wait<0>();
 
@@ -415,10 +606,13 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 8) {
-#define CC1D_GO(SI, SQ) \
-  return launch_dependent(fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kFwdStreamThreads>, ls.grid, dim3(kFwdStreamThreads), ls.smem, s, a)
-      if (silu) { if (seq) CC1D_GO(true, true); else CC1D_GO(true, false); }
-      else { if (seq) CC1D_GO(false, true); else CC1D_GO(false, false); }
+#define CC1D_GO(SI, SQ, EM) \
+  return launch_dependent(fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kFwdStreamThreads, EM>, ls.grid, dim3(kFwdStreamThreads), ls.smem, s, a)
+      if (ls.emit) {  // packed sequences: seq_idx is present
+        if (silu) CC1D_GO(true, true, true); else CC1D_GO(false, true, true);
+      }
+      if (silu) { if (seq) CC1D_GO(true, true, false); else CC1D_GO(true, false, false); }
+      else { if (seq) CC1D_GO(false, true, false); else CC1D_GO(false, false, false); }
 #undef CC1D_GO
     }
   } else if (ls.layout == kLayoutChannelLast) {

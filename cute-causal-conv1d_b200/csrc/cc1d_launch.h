@@ -31,6 +31,7 @@ struct LaunchShape {
   bool packet;  // 16-byte packets (alignment checked on the host) vs single elements
   bool silu;
   bool seq;
+  bool emit;    // streamed forward only: also write the varlen states (ConvArgs::states)
   size_t smem;
 };
 

@@ -201,6 +201,33 @@ typedef struct cc1d_varlen_states_params {
 
 cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* params, void* stream);
 
+/* ------------------------------------ forward that also writes the varlen states
+ * Fuses the two prefill calls of the reference, causal_conv1d_fn over packed sequences
+ * (causal_conv1d/causal_conv1d_interface.py:99-129 with seq_idx) followed by
+ * causal_conv1d_varlen_states (causal_conv1d/causal_conv1d_varlen.py:7-11), that hand
+ * the decode states to causal_conv1d_update.  Same results as
+ *     cc1d_fwd_launch(&params->fwd)
+ *     cc1d_varlen_states_launch({batch = nseq, dim, state_len, total_tokens = seqlen,
+ *                                x = fwd.x[0] as (seqlen, dim), cu_seqlens, states})
+ * but with seq_idx given, channel-last x and states whose channel stride is 1, the
+ * forward kernel stores each sequence's last state_len rows as it streams them, so x
+ * is read once and no second launch is made.  Other arguments take the two launches.
+ *   fwd         forward params; fwd.batch must be 1 (sequences packed along seqlen)
+ *   nseq        number of sequences
+ *   cu_seqlens  (nseq + 1,) int32 or int64, non-decreasing, cu[nseq] <= seqlen
+ *   states      (nseq, dim, state_len) output, x's dtype:
+ *               states[k, :, s] = x[0, :, cu[k+1] - state_len + s] if that position is
+ *               >= cu[k], else 0 (bit-exact copy)
+ */
+typedef struct cc1d_fwd_varlen_states_params {
+  cc1d_fwd_params fwd;
+  int64_t nseq, state_len;
+  cc1d_tensor cu_seqlens;
+  cc1d_tensor states;
+} cc1d_fwd_varlen_states_params;
+
+cc1d_status cc1d_fwd_varlen_states_launch(const cc1d_fwd_varlen_states_params* params, void* stream);
+
 /* ------------------------------------------------------------------- utility */
 /* Message of the last error on the calling thread ("" if none). */
 const char* cc1d_last_error(void);

@@ -59,6 +59,13 @@ def test_validation_errors_need_no_gpu():
     v.batch, v.dim, v.state_len = 1, 8, 2
     v.cu_seqlens.dtype = 0  # float cu_seqlens
     assert lib.cc1d_varlen_states_launch(ctypes.byref(v), None) == 2
+    f = _abi.FwdVarlenStatesParams()
+    f.fwd.batch, f.fwd.dim, f.fwd.seqlen, f.fwd.width = 2, 8, 4, 4  # packed sequences need batch 1
+    assert lib.cc1d_fwd_varlen_states_launch(ctypes.byref(f), None) == 1
+    assert b"batch == 1" in lib.cc1d_last_error()
+    f.fwd.batch, f.nseq, f.state_len = 1, 2, 3
+    f.cu_seqlens.dtype = 2  # bf16 cu_seqlens
+    assert lib.cc1d_fwd_varlen_states_launch(ctypes.byref(f), None) == 2
 
 
 def test_empty_problem_is_a_no_op():
@@ -85,6 +92,8 @@ int main(void) {
   P(cc1d_bwd_params, dweight); P(cc1d_bwd_params, workspace_bytes); P(cc1d_bwd_params, silu);
   P(cc1d_update_params, out); P(cc1d_update_params, silu);
   P(cc1d_varlen_states_params, states);
+  printf("cc1d_fwd_varlen_states_params %zu\n", sizeof(cc1d_fwd_varlen_states_params));
+  P(cc1d_fwd_varlen_states_params, nseq); P(cc1d_fwd_varlen_states_params, states);
   return 0;
 }
 """
@@ -114,6 +123,9 @@ def test_struct_layout_matches_ctypes(tmp_path):
         "cc1d_update_params.out": _abi.UpdateParams.out.offset,
         "cc1d_update_params.silu": _abi.UpdateParams.silu.offset,
         "cc1d_varlen_states_params.states": _abi.VarlenParams.states.offset,
+        "cc1d_fwd_varlen_states_params": ctypes.sizeof(_abi.FwdVarlenStatesParams),
+        "cc1d_fwd_varlen_states_params.nseq": _abi.FwdVarlenStatesParams.nseq.offset,
+        "cc1d_fwd_varlen_states_params.states": _abi.FwdVarlenStatesParams.states.offset,
     }
     assert {k: int(v) for k, v in got.items()} == py
 
@@ -124,7 +136,7 @@ def test_torch_ops_registered_with_fake_shapes():
     import causal_conv1d  # noqa: F401  (registers the operators)
     import torch
 
-    for name in ("fwd", "bwd", "update", "varlen_states"):
+    for name in ("fwd", "bwd", "update", "varlen_states", "fwd_varlen_states"):
         assert hasattr(torch.ops.causal_conv1d, name), name
     with FakeTensorMode():
         x = torch.empty(2, 512, 64).transpose(1, 2)  # (batch, dim, seqlen), channel-last
@@ -139,6 +151,11 @@ def test_torch_ops_registered_with_fake_shapes():
         xs = torch.empty(100, 64)
         cu = torch.empty(4, dtype=torch.int32)
         assert torch.ops.causal_conv1d.varlen_states(xs, cu, 3).shape == (3, 64, 3)
+        xp = torch.empty(1, 100, 64).transpose(1, 2)  # packed sequences, channel-last
+        sq = torch.empty(1, 100, dtype=torch.int32)
+        out, states = torch.ops.causal_conv1d.fwd_varlen_states(xp, w, b, sq, cu, 5, True)
+        assert out.shape == xp.shape and out.stride() == xp.stride()
+        assert states.shape == (3, 64, 5) and states.stride() == (320, 1, 64)
 
 
 def test_legacy_module_function_table():
