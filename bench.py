@@ -533,7 +533,7 @@ def run_extras(dev):
     import torch
 
     from causal_conv1d import causal_conv1d_update
-    from causal_conv1d.causal_conv1d_varlen import causal_conv1d_varlen_states
+    from causal_conv1d.causal_conv1d_varlen import causal_conv1d_fn_varlen_states, causal_conv1d_varlen_states
     from causal_conv1d.cpp_functions import causal_conv1d_bwd_function, causal_conv1d_fwd_function
 
     peak, _ = measured_peak()
@@ -594,6 +594,10 @@ def run_extras(dev):
     n = T * Dv
     us = graph_time([lambda: causal_conv1d_fwd_function(x, w4, b4, seq, None, None, True)] * 4, reps=3)
     res["config4_fwd_seq_idx"] = entry(2 * n * 2 + T * 4 + Dv * 20, us)
+    # the same forward also writing the 32 sequences' decode states (state_len 3) in one pass
+    cu4 = torch.nn.functional.pad(lens.cumsum(0), (1, 0)).to(torch.int32).to(dev)
+    us = graph_time([lambda: causal_conv1d_fn_varlen_states(x, w4, cu4, S, b4, seq, "silu")] * 4, reps=3)
+    res["config4_fwd_seq_idx_with_states"] = entry(2 * n * 2 + T * 4 + Dv * 20 + 33 * 4 + 32 * S * Dv * 2, us)
     us = graph_time([lambda: causal_conv1d_bwd_function(x, w4, b4, g, seq, None, None, None, False, True)] * 4,
                     reps=3)
     res["config4_bwd_seq_idx"] = entry(3 * n * 2 + T * 4 + Dv * 40, us)
