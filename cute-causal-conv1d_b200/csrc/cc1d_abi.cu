@@ -630,6 +630,17 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   if (B == 0 || D == 0 || T == 0) return CC1D_OK;
   if (!p->x.data || !p->conv_state.data || !p->weight.data || !p->out.data)
     return fail(CC1D_ERR_VALUE, "x, conv_state, weight and out are required");
+  // A shift update (no circular buffer, state_len == W-1) of a state whose entries per
+  // channel are contiguous and channels state_len apart: whole 8-byte blocks of
+  // channels' histories (update_shift_kernel).
+  const int ch = 8 / elem_size(p->x.dtype);
+  auto aligned8 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 7u) == 0; };
+  auto vec8 = [&](const cc1d_tensor& t, int64_t n0, int64_t n2) {
+    return t.stride[1] == 1 && aligned8(t.data) && stride_ok(t.stride[0], n0, ch) && stride_ok(t.stride[2], n2, ch);
+  };
+  const bool shift = !p->cache_seqlens.data && S == W - 1 && D % ch == 0 && p->conv_state.stride[2] == 1 &&
+                     p->conv_state.stride[1] == S && aligned8(p->conv_state.data) &&
+                     stride_ok(p->conv_state.stride[0], p->state_batch, ch) && vec8(p->x, B, T) && vec8(p->out, B, T);
   const int vec = 8 / elem_size(p->x.dtype);  // 8-byte packets along dim
   auto ok = [&](const cc1d_tensor& t, int64_t n0, int64_t n2) {
     return t.stride[1] == 1 && (reinterpret_cast<uintptr_t>(t.data) % 8) == 0 && stride_ok(t.stride[0], n0, vec) &&
@@ -652,8 +663,21 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   a.indices = static_cast<const int32_t*>(p->conv_state_indices.data);
   a.indices_stride = p->conv_state_indices.stride[0];
   a.silu = p->silu;
-  a.weight_vec = packet && (vec * W) % 4 == 0 && p->weight.dtype == CC1D_FLOAT32 && p->weight.stride[1] == 1 &&
-                 p->weight.stride[0] == W && aligned16(p->weight.data);
+  const bool w_flat = p->weight.dtype == CC1D_FLOAT32 && p->weight.stride[1] == 1 && p->weight.stride[0] == W &&
+                      aligned16(p->weight.data);
+  if (shift) {
+    a.weight_vec = w_flat;  // 8-byte weight pairs: d0 * W is even
+    const int64_t nbx = (D / ch + 31) / 32;
+    auto blocks_for = [&](int rows) { return nbx * ((B + 8 * rows - 1) / (8 * rows)); };
+    int rows = kUpdateRows;  // fewer rows per thread while the grid is under two CTAs per SM
+    while (rows > 1 && blocks_for(rows) < 2 * (int64_t)sm_count()) rows /= 2;
+    cudaError_t e = launch_update_shift(p->x.dtype, a, (int)W, rows, dim3((unsigned)blocks_for(rows)),
+                                        static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d update launch");
+    g_launches.fetch_add(1);
+    return CC1D_OK;
+  }
+  a.weight_vec = packet && (vec * W) % 4 == 0 && w_flat;
   const int64_t nv = (D + (packet ? vec : 1) - 1) / (packet ? vec : 1);
   const int64_t blocks = ((nv + 31) / 32) * ((B + 8 * kUpdateRows - 1) / (8 * kUpdateRows));
   cudaError_t e = launch_update(p->x.dtype, a, (int)W, packet, dim3((unsigned)std::max<int64_t>(1, blocks)),

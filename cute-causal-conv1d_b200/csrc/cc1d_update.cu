@@ -178,6 +178,114 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
   }
 }
 
+// Shift update of a (batch, dim, state_len) state stored with its state_len entries per
+// channel contiguous (stride 1) and channels state_len apart, for state_len == W-1 and
+// no circular buffer.  The states of CH consecutive channels (8 bytes of x) are then one
+// contiguous block of W-1 8-byte vectors, so a thread moves its channels' history with
+// W-1 vector loads and stores instead of per-element accesses, and a warp covers 32
+// consecutive blocks.  A thread takes BR batch rows and issues the
+// loads of all of them (x, row index, state block) before using any.  The new state is
+// assembled from the raw input elements (bit exact).
+template <typename T, int W, int BR>
+__global__ void __launch_bounds__(kThreads) update_shift_kernel(const UpdateArgs a) {
+  grid_dependency_wait();  // launched as a programmatic dependent launch
+  constexpr int CH = 8 / sizeof(T);  // channels per thread
+  constexpr int S = W - 1;            // state entries per channel
+  using Pk = Packet<T, CH>;
+  const int tx = threadIdx.x & 31;
+  const int ty = threadIdx.x >> 5;
+  const int64_t nv = a.dim / CH;
+  const int64_t nbx = (nv + 31) / 32;
+  const int64_t cv = (blockIdx.x % nbx) * 32 + tx;
+  const int64_t b0 = ((blockIdx.x / nbx) * (kThreads / 32) + ty) * BR;
+  if (cv >= nv || b0 >= a.batch) return;
+  const int64_t d0 = cv * CH;
+  const int T_len = static_cast<int>(a.seqlen);
+
+  int row[BR];
+  bool ok[BR];
+  Pk x0[BR], blk[BR][S];
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    const int64_t b = b0 + r;
+    ok[r] = b < a.batch;
+    if (ok[r]) x0[r] = ld_packet<T, CH>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0);
+    row[r] = (ok[r] && a.indices) ? a.indices[b * a.indices_stride] : static_cast<int>(b);
+  }
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    if (!ok[r] || row[r] < 0) continue;
+    const T* sp = static_cast<const T*>(a.state.data) + (int64_t)row[r] * a.state.s0 + d0 * S;
+#pragma unroll
+    for (int q = 0; q < S; ++q) blk[r][q] = ld_packet<T, CH>(sp + q * CH);
+  }
+
+  float wv[W][CH], bv[CH];
+  if (a.weight_vec) {  // contiguous fp32 (dim, W): this thread's CH*W weights are adjacent
+    const float2* wp = reinterpret_cast<const float2*>(static_cast<const float*>(a.weight.data) + d0 * W);
+#pragma unroll
+    for (int q = 0; q < CH * W / 2; ++q) {
+      const float2 f = __ldg(wp + q);
+      wv[(2 * q) % W][(2 * q) / W] = f.x;
+      wv[(2 * q + 1) % W][(2 * q + 1) / W] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        wv[w][c] = load_any(a.weight.data, a.weight.dtype, (d0 + c) * a.weight.s0 + w * a.weight.s1);
+  }
+#pragma unroll
+  for (int c = 0; c < CH; ++c) bv[c] = a.bias.data ? load_any(a.bias.data, a.bias.dtype, (d0 + c) * a.bias.s0) : 0.f;
+
+#pragma unroll
+  for (int r = 0; r < BR; ++r) {
+    if (!ok[r]) continue;
+    const int64_t b = b0 + r;
+    const T* xp = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0;
+    T* op = static_cast<T*>(a.out.data) + b * a.out.s0 + d0;
+    if (row[r] < 0) {  // padded batch row: zero output, state untouched
+      float z[CH];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) z[c] = 0.f;
+      for (int t = 0; t < T_len; ++t) st_packet<T, CH>(op + t * a.out.s2, pack<T, CH>(z));
+      continue;
+    }
+    // the history of channel c is elements c*S .. c*S+S-1 of the block
+    T hr[S][CH];
+#pragma unroll
+    for (int e = 0; e < S * CH; ++e) hr[e % S][e / S] = blk[r][e / CH].v[e % CH];
+    for (int t = 0; t < T_len; ++t) {
+      const Pk xr = t == 0 ? x0[r] : ld_packet<T, CH>(xp + t * a.x.s2);
+      float acc[CH];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        float s = bv[c];
+#pragma unroll
+        for (int w = 0; w < S; ++w) s = fmaf(wv[w][c], to_f32(hr[w][c]), s);
+        s = fmaf(wv[W - 1][c], to_f32(xr.v[c]), s);
+        if (a.silu) s = silu_fwd<T>(s);
+        acc[c] = s;
+      }
+      st_packet<T, CH>(op + t * a.out.s2, pack<T, CH>(acc));
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+#pragma unroll
+        for (int k = 0; k + 1 < S; ++k) hr[k][c] = hr[k + 1][c];
+        hr[S - 1][c] = xr.v[c];
+      }
+    }
+    // the new state: the last S entries of [old | x], back in block order
+    Pk nb[S];
+#pragma unroll
+    for (int e = 0; e < S * CH; ++e) nb[e / CH].v[e % CH] = hr[e % S][e / S];
+    T* sp = static_cast<T*>(a.state.data) + (int64_t)row[r] * a.state.s0 + d0 * S;
+#pragma unroll
+    for (int q = 0; q < S; ++q) st_packet<T, CH>(sp + q * CH, nb[q]);
+  }
+}
+
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kThreads) varlen_states_kernel(const VarlenArgs a) {
   grid_dependency_wait();  // launched as a programmatic dependent launch
@@ -236,6 +344,34 @@ cudaError_t launch_update(int dtype, const UpdateArgs& a, int width, bool packet
     case CC1D_FLOAT32: return launch_update_t<float>(a, width, packet, grid, s);
     case CC1D_FLOAT16: return launch_update_t<__half>(a, width, packet, grid, s);
     case CC1D_BFLOAT16: return launch_update_t<__nv_bfloat16>(a, width, packet, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T, int W>
+static cudaError_t launch_shift_w(const UpdateArgs& a, int rows, dim3 grid, cudaStream_t s) {
+  switch (rows) {
+    case 1: return launch_dependent(update_shift_kernel<T, W, 1>, grid, dim3(kThreads), 0, s, a);
+    case 2: return launch_dependent(update_shift_kernel<T, W, 2>, grid, dim3(kThreads), 0, s, a);
+    default: return launch_dependent(update_shift_kernel<T, W, 4>, grid, dim3(kThreads), 0, s, a);
+  }
+}
+
+template <typename T>
+static cudaError_t launch_shift_t(const UpdateArgs& a, int width, int rows, dim3 grid, cudaStream_t s) {
+  switch (width) {
+    case 2: return launch_shift_w<T, 2>(a, rows, grid, s);
+    case 3: return launch_shift_w<T, 3>(a, rows, grid, s);
+    case 4: return launch_shift_w<T, 4>(a, rows, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_update_shift(int dtype, const UpdateArgs& a, int width, int rows, dim3 grid, cudaStream_t s) {
+  switch (dtype) {
+    case CC1D_FLOAT32: return launch_shift_t<float>(a, width, rows, grid, s);
+    case CC1D_FLOAT16: return launch_shift_t<__half>(a, width, rows, grid, s);
+    case CC1D_BFLOAT16: return launch_shift_t<__nv_bfloat16>(a, width, rows, grid, s);
     default: return cudaErrorInvalidValue;
   }
 }

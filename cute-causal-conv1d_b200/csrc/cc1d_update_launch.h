@@ -18,6 +18,7 @@ struct UpdateArgs {
   int64_t indices_stride;
   int32_t silu;
   int32_t weight_vec;  // weight is contiguous fp32 (dim, W), 16-byte aligned, and packets are used
+                      // (update_shift_kernel: contiguous fp32 (dim, W), 16-byte aligned)
 };
 
 struct VarlenArgs {
@@ -30,5 +31,7 @@ struct VarlenArgs {
 
 cudaError_t launch_update(int dtype, const UpdateArgs& a, int width, bool packet, dim3 grid, cudaStream_t s);
 cudaError_t launch_varlen_states(int dtype, const VarlenArgs& a, bool packet, dim3 grid, cudaStream_t s);
+// update_shift_kernel with `rows` (1, 2 or 4) batch rows per thread
+cudaError_t launch_update_shift(int dtype, const UpdateArgs& a, int width, int rows, dim3 grid, cudaStream_t s);
 
 }  // namespace cc1d

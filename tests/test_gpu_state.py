@@ -90,6 +90,34 @@ def test_update_grid(dim, width, seqlen, dt, circular, mode):
     run_update_vs_oracle(gen, 64, dim, seqlen, width, state_len, dt, circular, mode, channel_last)
 
 
+@pytest.mark.parametrize("dim", [2048, 2052, 2050])
+@pytest.mark.parametrize("width", [2, 3, 4])
+@pytest.mark.parametrize("seqlen", [1, 2, 5])
+@pytest.mark.parametrize("dt", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("mode", ["plain", "gather", "padding"])
+def test_update_shift_contiguous_state(dim, width, seqlen, dt, mode):
+    """(batch, dim, W-1) state with contiguous entries and no circular buffer (config 3a
+    as BASELINE.json gives it): whole channel blocks of the history per thread, bit-exact
+    state.  dim 2050 is not a whole number of 8-byte channel blocks for 16-bit types and
+    takes the per-channel kernel."""
+    gen = torch.Generator().manual_seed(dim + 7 * width + seqlen)
+    run_update_vs_oracle(gen, 64, dim, seqlen, width, width - 1, dt, False, mode, False)
+
+
+def test_update_shift_contiguous_state_strided_weight():
+    """The same kernel with weights that are not one contiguous fp32 (dim, W) block."""
+    gen = torch.Generator().manual_seed(9)
+    x = torch.randn(16, 512, 1, generator=gen).to(torch.bfloat16)
+    state = torch.randn(16, 512, 3, generator=gen).to(torch.bfloat16)
+    w = torch.rand(4, 512, generator=gen) - 0.5
+    eo, es = O.update(to_storage(x), "bfloat16", to_storage(state), w.t().contiguous().numpy(), "float32", None,
+                      silu=True)
+    sg = state.cuda()
+    out = causal_conv1d_update(x.cuda(), sg, w.cuda().t(), None, activation="silu")
+    assert_close(out, eo, "bfloat16", PARITY["bfloat16"], "out")
+    assert np.array_equal(to_storage(sg), es)
+
+
 @pytest.mark.parametrize("channel_last", [True, False])
 def test_update_squeezed_2d_input(channel_last):
     gen = torch.Generator().manual_seed(3)
