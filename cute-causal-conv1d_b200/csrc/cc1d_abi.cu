@@ -667,12 +667,8 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
                       aligned16(p->weight.data);
   if (shift) {
     a.weight_vec = w_flat;  // 8-byte weight pairs: d0 * W is even
-    const int64_t nbx = (D / ch + 31) / 32;
-    auto blocks_for = [&](int rows) { return nbx * ((B + 8 * rows - 1) / (8 * rows)); };
-    int rows = kUpdateRows;  // fewer rows per thread while the grid is under two CTAs per SM
-    while (rows > 1 && blocks_for(rows) < 2 * (int64_t)sm_count()) rows /= 2;
-    cudaError_t e = launch_update_shift(p->x.dtype, a, (int)W, rows, dim3((unsigned)blocks_for(rows)),
-                                        static_cast<cudaStream_t>(stream));
+    const int64_t blocks = ((D / ch + 31) / 32) * ((B + 8 * kUpdateRows - 1) / (8 * kUpdateRows));
+    cudaError_t e = launch_update_shift(p->x.dtype, a, (int)W, dim3((unsigned)blocks), static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d update launch");
     g_launches.fetch_add(1);
     return CC1D_OK;

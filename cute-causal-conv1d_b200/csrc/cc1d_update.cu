@@ -348,30 +348,22 @@ cudaError_t launch_update(int dtype, const UpdateArgs& a, int width, bool packet
   }
 }
 
-template <typename T, int W>
-static cudaError_t launch_shift_w(const UpdateArgs& a, int rows, dim3 grid, cudaStream_t s) {
-  switch (rows) {
-    case 1: return launch_dependent(update_shift_kernel<T, W, 1>, grid, dim3(kThreads), 0, s, a);
-    case 2: return launch_dependent(update_shift_kernel<T, W, 2>, grid, dim3(kThreads), 0, s, a);
-    default: return launch_dependent(update_shift_kernel<T, W, 4>, grid, dim3(kThreads), 0, s, a);
-  }
-}
-
 template <typename T>
-static cudaError_t launch_shift_t(const UpdateArgs& a, int width, int rows, dim3 grid, cudaStream_t s) {
+static cudaError_t launch_shift_t(const UpdateArgs& a, int width, dim3 grid, cudaStream_t s) {
+  constexpr int BR = kUpdateRows;
   switch (width) {
-    case 2: return launch_shift_w<T, 2>(a, rows, grid, s);
-    case 3: return launch_shift_w<T, 3>(a, rows, grid, s);
-    case 4: return launch_shift_w<T, 4>(a, rows, grid, s);
+    case 2: return launch_dependent(update_shift_kernel<T, 2, BR>, grid, dim3(kThreads), 0, s, a);
+    case 3: return launch_dependent(update_shift_kernel<T, 3, BR>, grid, dim3(kThreads), 0, s, a);
+    case 4: return launch_dependent(update_shift_kernel<T, 4, BR>, grid, dim3(kThreads), 0, s, a);
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t launch_update_shift(int dtype, const UpdateArgs& a, int width, int rows, dim3 grid, cudaStream_t s) {
+cudaError_t launch_update_shift(int dtype, const UpdateArgs& a, int width, dim3 grid, cudaStream_t s) {
   switch (dtype) {
-    case CC1D_FLOAT32: return launch_shift_t<float>(a, width, rows, grid, s);
-    case CC1D_FLOAT16: return launch_shift_t<__half>(a, width, rows, grid, s);
-    case CC1D_BFLOAT16: return launch_shift_t<__nv_bfloat16>(a, width, rows, grid, s);
+    case CC1D_FLOAT32: return launch_shift_t<float>(a, width, grid, s);
+    case CC1D_FLOAT16: return launch_shift_t<__half>(a, width, grid, s);
+    case CC1D_BFLOAT16: return launch_shift_t<__nv_bfloat16>(a, width, grid, s);
     default: return cudaErrorInvalidValue;
   }
 }

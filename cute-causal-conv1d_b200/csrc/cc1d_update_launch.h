@@ -31,7 +31,7 @@ struct VarlenArgs {
 
 cudaError_t launch_update(int dtype, const UpdateArgs& a, int width, bool packet, dim3 grid, cudaStream_t s);
 cudaError_t launch_varlen_states(int dtype, const VarlenArgs& a, bool packet, dim3 grid, cudaStream_t s);
-// update_shift_kernel with `rows` (1, 2 or 4) batch rows per thread
-cudaError_t launch_update_shift(int dtype, const UpdateArgs& a, int width, int rows, dim3 grid, cudaStream_t s);
+// update_shift_kernel (kUpdateRows batch rows per thread)
+cudaError_t launch_update_shift(int dtype, const UpdateArgs& a, int width, dim3 grid, cudaStream_t s);
 
 }  // namespace cc1d
