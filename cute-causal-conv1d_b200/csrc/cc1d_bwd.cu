@@ -280,8 +280,10 @@ struct BwdWalk {
   int sw[W - 1];
 
   // One row: g = dout * silu'(p) at this row; optional dweight/dbias accumulation;
-  // dx of the row W-1 earlier into `dxv`.  Windows advance by one row.
-  template <bool ACC, bool EMIT>
+  // dx of the row W-1 earlier into `dxv`.  Windows advance by one row.  MASK applies the
+  // seq_idx masks; a row whose window rows all carry its own non-negative seq_idx needs
+  // none (every mask is 1).
+  template <bool ACC, bool EMIT, bool MASK = SEQ>
   __device__ __forceinline__ void step(const float2 (&xc)[H], const float2 (&gc)[H], int scur, bool acc,
                                        float2 (&dxv)[H]) {
     float2 g[H];
@@ -293,15 +295,15 @@ struct BwdWalk {
 #pragma unroll
         for (int w = 0; w < W - 1; ++w) {
           float2 xin = xw[w][i];
-          if constexpr (SEQ) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
+          if constexpr (MASK) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
           p = ffma2(wv[w][i], xin, p);
         }
         p = ffma2(wv[W - 1][i], xc[i], p);
-        if constexpr (SEQ) p = (scur >= 0) ? p : make_float2(0.f, 0.f);
+        if constexpr (MASK) p = (scur >= 0) ? p : make_float2(0.f, 0.f);
         if constexpr (HALF) gv = fmul2(gv, silu_grad_half_arg2_x2(p));
         else gv = fmul2(gv, silu_grad2(p));
       }
-      if constexpr (SEQ) gv = (scur >= 0) ? gv : make_float2(0.f, 0.f);
+      if constexpr (MASK) gv = (scur >= 0) ? gv : make_float2(0.f, 0.f);
       g[i] = gv;
     }
     if (ACC && acc) {
@@ -311,7 +313,7 @@ struct BwdWalk {
 #pragma unroll
         for (int w = 0; w < W - 1; ++w) {
           float2 xin = xw[w][i];
-          if constexpr (SEQ) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
+          if constexpr (MASK) xin = (sw[w] == scur) ? xin : make_float2(0.f, 0.f);
           dw[w][i] = ffma2(g[i], xin, dw[w][i]);
         }
         dw[W - 1][i] = ffma2(g[i], xc[i], dw[W - 1][i]);
@@ -324,11 +326,11 @@ struct BwdWalk {
 #pragma unroll
         for (int k = 0; k < W - 1; ++k) {
           float2 gk = gw[k][i];
-          if constexpr (SEQ) gk = (sw[0] == sw[k]) ? gk : make_float2(0.f, 0.f);
+          if constexpr (MASK) gk = (sw[0] == sw[k]) ? gk : make_float2(0.f, 0.f);
           s = ffma2(wv[W - 1 - k][i], gk, s);
         }
         float2 gk = g[i];
-        if constexpr (SEQ) gk = (sw[0] == scur) ? gk : make_float2(0.f, 0.f);
+        if constexpr (MASK) gk = (sw[0] == scur) ? gk : make_float2(0.f, 0.f);
         dxv[i] = ffma2(wv[0][i], gk, s);
       }
     }
@@ -502,11 +504,67 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
     }
     // steady: rows W-1 .. nmain-1 in unrolled blocks of P (compile-time slots), then the rest
     int j = W - 1;
-    for (; j + P <= nmain; j += P) {
+    bool plain_blocks = true;
+    if constexpr (SEQ) {
+      // Warps whose 32 lanes all hold channels read the seq_idx of 32 steady rows at a
+      // time, one per lane (steady row W-1 + r in lane r % 32 of chunk r / 32), the next
+      // chunk one chunk ahead.  A block whose P rows and W-1 window rows all carry one
+      // non-negative id runs the step without masks; any other block goes row by row
+      // with the masks.  The result is the same either way.
+      if (pb * 32 + 32 <= a.nv) {
+        plain_blocks = false;
+        constexpr unsigned FULL = 0xffffffffu;
+        const int* ids = srow + (l0 + W - 1) * a.seq_idx.s1;
+        const int nsteady = nmain - (W - 1);
+        auto load_ids = [&](int r0) {
+          const int r = r0 + lane;
+          return r < nsteady ? __ldg(ids + static_cast<int64_t>(r) * a.seq_idx.s1) : -1;
+        };
+        int cur = load_ids(0), nxt = load_ids(32);
+        int k = 0;  // first row of the block within the chunk
+        for (; j + P <= nmain; j += P) {
+          const int v = st.sw[0];
+          bool same = v >= 0;
 #pragma unroll
-      for (int u = 0; u < P; ++u) {
-        prefetch(j + u, (u + W - 1 + P - 1) % P);
-        steady_row(xring[((u + W - 1) % P) * NT], gring[((u + W - 1) % P) * NT]);
+          for (int w = 1; w < W - 1; ++w) same = same && st.sw[w] == v;
+          same = __all_sync(FULL, same && (static_cast<unsigned>(lane - k) >= static_cast<unsigned>(P) || cur == v));
+          if (same) {
+#pragma unroll
+            for (int u = 0; u < P; ++u) {
+              prefetch(j + u, (u + W - 1 + P - 1) % P);
+              const Pk& rx = xring[((u + W - 1) % P) * NT];
+              const Pk& rg = gring[((u + W - 1) % P) * NT];
+              float2 xc[H], gc[H];
+              unpack2<T, VEC>(rx, xc);
+              unpack2<T, VEC>(rg, gc);
+              float2 dxv[H];
+              st.template step<true, true, false>(xc, gc, v, true, dxv);
+              st_packet<T, VEC>(dxptr, pack2<T, VEC>(dxv));
+              dxptr += sd;
+            }
+            sptr += P * a.seq_idx.s1;
+          } else {
+            for (int u = 0; u < P; ++u) {  // rare: row by row, reading each row's id
+              prefetch(j + u, (j + u + P - 1) % P);
+              steady_row(xring[((j + u) % P) * NT], gring[((j + u) % P) * NT]);
+            }
+          }
+          k += P;
+          if (k == 32) {
+            k = 0;
+            cur = nxt;
+            nxt = load_ids(j + P - (W - 1) + 32);
+          }
+        }
+      }
+    }
+    if (plain_blocks) {
+      for (; j + P <= nmain; j += P) {
+#pragma unroll
+        for (int u = 0; u < P; ++u) {
+          prefetch(j + u, (u + W - 1 + P - 1) % P);
+          steady_row(xring[((u + W - 1) % P) * NT], gring[((u + W - 1) % P) * NT]);
+        }
       }
     }
     for (; j < nmain; ++j) {

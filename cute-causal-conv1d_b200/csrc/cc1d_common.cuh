@@ -382,6 +382,20 @@ struct SeqFeed {
     }
     return v;
   }
+  // Whether the next n rows (n divides 32, k a multiple of n) all carry the value v.
+  __device__ __forceinline__ bool next_all(int lane, int n, int v) const {
+    return __all_sync(0xffffffffu, static_cast<unsigned>(lane - k) >= static_cast<unsigned>(n) || cur == v);
+  }
+  // Passes over the next n rows (n divides 32, k a multiple of n).
+  __device__ __forceinline__ void skip(int lane, int n) {
+    k += n;
+    if (k == 32) {
+      k = 0;
+      cur = nxt;
+      nxt = load(lane);
+      pos += 32;
+    }
+  }
 };
 
 // Weight and bias of VEC consecutive channels, as fp32.

@@ -371,6 +371,29 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
     for (int i = 0; i < H; ++i) xw[W - 2][i] = xc[i];
     sw[W - 2] = scur;
   };
+  // A row whose window rows all carry its own non-negative seq_idx: every mask is 1.
+  [[maybe_unused]] auto row_same = [&](const Pk& raw) {
+    float2 xc[H];
+    unpack2<T, VEC>(raw, xc);
+    float2 acc[H];
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      float2 s = bv[i];
+#pragma unroll
+      for (int w = 0; w < W - 1; ++w) s = ffma2(wv[w][i], xw[w][i], s);
+      s = ffma2(wv[W - 1][i], xc[i], s);
+      if constexpr (SILU) s = HALF_ARG ? silu_half_arg2(s) : silu_exact2(s);
+      acc[i] = s;
+    }
+    st_packet<T, VEC>(optr, pack2<T, VEC>(acc));
+    optr += so;
+#pragma unroll
+    for (int k = 0; k < W - 2; ++k)
+#pragma unroll
+      for (int i = 0; i < H; ++i) xw[k][i] = xw[k + 1][i];
+#pragma unroll
+    for (int i = 0; i < H; ++i) xw[W - 2][i] = xc[i];
+  };
   int j0 = 0;
   if constexpr (EMIT) {
     // The plain loop below, written out again (the same text keeps the same code), up
@@ -380,6 +403,24 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
     for (;;) {
       const int64_t plain_end = min(static_cast<int64_t>(n), static_cast<int64_t>(emit.lo) - l0);
       for (; j0 + P <= plain_end; j0 += P) {
+        if (full_warp) {  // one non-negative id over the block and its window: no masks
+          const int v = sw[0];
+          bool same = v >= 0;
+#pragma unroll
+          for (int w = 1; w < W - 1; ++w) same = same && sw[w] == v;
+          if (same && seq.next_all(lane, P, v)) {  // `same` is the same in every lane
+#pragma unroll
+            for (int u = 0; u < P; ++u) {
+              cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
+              xsrc += sx;
+              cp_async_commit();
+              cp_async_wait<P - 1>();
+              row_same(ring[u * NT]);
+            }
+            seq.skip(lane, P);
+            continue;
+          }
+        }
 #pragma unroll
         for (int u = 0; u < P; ++u) {
           cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
@@ -423,8 +464,30 @@ __global__ void __launch_bounds__(NT) fwd_stream_kernel(const ConvArgs a) {
       row(ring[(j % P) * NT]);
     }
   } else {
-    // full blocks of P rows: compile-time ring slots, predicated prefetch, no branches
+    // full blocks of P rows: compile-time ring slots, predicated prefetch, no branches.
+    // With seq_idx, a full warp runs a block whose P rows and W-1 window rows all carry
+    // one non-negative id without the masks (the same result).
     for (; j0 + P <= n; j0 += P) {
+      if constexpr (SEQ) {
+        if (full_warp) {
+          const int v = sw[0];
+          bool same = v >= 0;
+#pragma unroll
+          for (int w = 1; w < W - 1; ++w) same = same && sw[w] == v;
+          if (same && seq.next_all(lane, P, v)) {  // `same` is the same in every lane
+#pragma unroll
+            for (int u = 0; u < P; ++u) {
+              cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
+              xsrc += sx;
+              cp_async_commit();
+              cp_async_wait<P - 1>();
+              row_same(ring[u * NT]);
+            }
+            seq.skip(lane, P);
+            continue;
+          }
+        }
+      }
 #pragma unroll
       for (int u = 0; u < P; ++u) {
         cp_async_packet<sizeof(Pk)>(ring + ((u + P - 1) % P) * NT, xsrc, j0 + u + P - 1 < n);
