@@ -117,21 +117,34 @@ __device__ __forceinline__ float select_of(const float (&v)[N], int64_t idx) {
   return r;
 }
 
-// x window of one lane: xs[k] = x at p0 - (W-1) + k (k < VEC + W - 1); carry becomes
-// the last W-1 values of lane 31.
-template <int W, int VEC>
+// x window of one lane: xs[k] = x at p0 - (W-1) + k (k < VEC + W - 1); carry (used by
+// lane 0) becomes the last W-1 values of lane 31.  ROTATE: one rotation by a lane serves
+// both (lane l > 0 receives the tail of lane l-1, lane 0 the tail of lane 31 for the
+// next step); otherwise a shift up plus a broadcast of lane 31 (the forward keeps this
+// form: the rotation saved it nothing).
+template <int W, int VEC, bool ROTATE>
 __device__ __forceinline__ void lane_window(const float (&xe)[VEC], float (&carry)[W - 1], int lane,
                                             float (&xs)[VEC + W - 1]) {
   constexpr unsigned FULL = 0xffffffffu;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) xs[W - 1 + i] = xe[i];
+  if constexpr (ROTATE) {
+    const int left = (lane + 31) & 31;
 #pragma unroll
-  for (int j = 0; j < W - 1; ++j) {
-    const float v = __shfl_up_sync(FULL, xe[VEC - (W - 1) + j], 1);
-    xs[j] = lane == 0 ? carry[j] : v;
+    for (int j = 0; j < W - 1; ++j) {
+      const float v = __shfl_sync(FULL, xe[VEC - (W - 1) + j], left);
+      xs[j] = lane == 0 ? carry[j] : v;
+      carry[j] = v;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      const float v = __shfl_up_sync(FULL, xe[VEC - (W - 1) + j], 1);
+      xs[j] = lane == 0 ? carry[j] : v;
+    }
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) carry[j] = __shfl_sync(FULL, xe[VEC - (W - 1) + j], 31);
   }
-#pragma unroll
-  for (int j = 0; j < W - 1; ++j) carry[j] = __shfl_sync(FULL, xe[VEC - (W - 1) + j], 31);
 }
 
 // Producer side of the walk: streams this lane's packet of consecutive steps (running
@@ -245,7 +258,7 @@ __global__ void __launch_bounds__(NT) fwd_rowwalk_kernel(const ConvArgs a) {
       float xe[VEC], xs[VEC + W - 1];
       unpack<T, VEC>(ring[slot * NT], xe);
       slot = slot + 1 == P ? 0 : slot + 1;
-      lane_window<W, VEC>(xe, carry, lane, xs);
+      lane_window<W, VEC, false>(xe, carry, lane, xs);
       // fp32 pairs hold elements (m, m + VEC/2): a window shifted by w is again a pair
       // of the same layout, so no register has to be moved to form FFMA2 operands
       float o[VEC];
@@ -365,16 +378,20 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
 
   // dx of one step (g values gs, lane position pos, output pdx) given the first W-1 g
   // values of the step to its right (nxt, read from lane 0); on the row's last step
-  // (last) it adds dfinal_states.
+  // (last) it adds dfinal_states.  The right halo comes from one rotation by a lane:
+  // rot_nxt (nxt of lane l+1) serves lane 31 now, and lanes 0..30 at the next step,
+  // whose own g is this step's nxt; rot_gs holds that rotation of gs from the step before.
+  const int right = (lane + 1) & 31;
+  float rot_gs[W - 1];
   auto emit = [&](T* pdx, int64_t pos, const float (&gs)[VEC], const float (&nxt)[VEC], bool last) {
     float G[VEC + W - 1];
 #pragma unroll
     for (int i = 0; i < VEC; ++i) G[i] = gs[i];
 #pragma unroll
     for (int j = 0; j < W - 1; ++j) {
-      const float v = __shfl_down_sync(FULL, gs[j], 1);
-      const float h = __shfl_sync(FULL, nxt[j], 0);
-      G[VEC + j] = lane == 31 ? h : v;
+      const float h = __shfl_sync(FULL, nxt[j], right);
+      G[VEC + j] = lane == 31 ? h : rot_gs[j];
+      rot_gs[j] = h;
     }
     float dxe[VEC];
 #pragma unroll
@@ -407,7 +424,7 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
     unpack<T, VEC>(xring[slot * NT], xe);
     unpack<T, VEC>(gring[slot * NT], de);
     slot = slot + 1 == P ? 0 : slot + 1;
-    lane_window<W, VEC>(xe, carry, lane, xs);
+    lane_window<W, VEC, true>(xe, carry, lane, xs);
 #pragma unroll
     for (int m = 0; m < H2; ++m) {
       float2 gv = make_float2(de[m], de[m + H2]);
@@ -448,10 +465,16 @@ __global__ void __launch_bounds__(NT) bwd_rowwalk_kernel(const ConvArgs a) {
     int64_t pos = (int64_t)cc.step * S + lane * VEC;
     T* pdx = row_of<T>(a.dx, cc) + pos;
     float gprev[VEC];
+#pragma unroll 2
     for (int k = 0; k < seg; ++k) {
       float xs[VEC + W - 1], g[VEC];
       next_g(xs, g);
-      if (k > 0) emit(pdx - S, pos - S, gprev, g, false);
+      if (k > 0) {
+        emit(pdx - S, pos - S, gprev, g, false);
+      } else {  // the first step of the piece: seed the rotated right halo
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j) rot_gs[j] = __shfl_sync(FULL, g[j], right);
+      }
       // dinitial_states: dx at positions -(W-1) .. -1 of the row, from g at 0 .. W-2
       if (STATES && k == 0 && cc.step == 0 && a.dinit.data && lane == 0) {
 #pragma unroll
