@@ -137,6 +137,32 @@ def _check(status: int) -> None:
         raise _ERRORS.get(status, RuntimeError)(msg or f"causal_conv1d error {status}")
 
 
+def _expect(name: str, t: torch.Tensor | None, shape: tuple) -> None:
+    """Reject a tensor whose shape is not the one the kernels will index.  The C ABI
+    receives pointers and strides only, so a tensor that is too small would otherwise be
+    read or written out of bounds."""
+    if t is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+
+
+def _expect_dims(name: str, t: torch.Tensor, ndim: int) -> None:
+    if t.dim() != ndim:
+        raise ValueError(f"{name} must have {ndim} dimensions, got shape {tuple(t.shape)}")
+
+
+def _conv_shapes(x, weight, bias, seq_idx, initial_states):
+    """(batch, dim, seqlen, width) of a conv call after checking its input shapes."""
+    _expect_dims("x", x, 3)
+    _expect_dims("weight", weight, 2)
+    B, D, L = x.shape
+    W = weight.shape[1]
+    _expect("weight", weight, (D, W))
+    _expect("bias", bias, (D,))
+    _expect("seq_idx", seq_idx, (B, L))
+    _expect("initial_states", initial_states, (B, D, W - 1))
+    return B, D, L, W
+
+
 def _device_of(*tensors: torch.Tensor | None) -> torch.device:
     dev = None
     for t in tensors:
@@ -174,6 +200,9 @@ class _Guard:
 
 
 def fwd(x, weight, bias, seq_idx, initial_states, final_states, out, silu: bool) -> None:
+    B, D, L, W = _conv_shapes(x, weight, bias, seq_idx, initial_states)
+    _expect("final_states", final_states, (B, D, W - 1))
+    _expect("out", out, (B, D, L))
     lib = load_library()
     dev = _device_of(x, weight, bias, seq_idx, initial_states, final_states, out)
     p = FwdParams(
@@ -187,6 +216,13 @@ def fwd(x, weight, bias, seq_idx, initial_states, final_states, out, silu: bool)
 
 def bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial_states,
         dweight_f32, dbias_f32, silu: bool, workspace: torch.Tensor | None = None) -> None:
+    B, D, L, W = _conv_shapes(x, weight, bias, seq_idx, initial_states)
+    for name, t in (("dout", dout), ("dx", dx)):
+        _expect(name, t, (B, D, L))
+    for name, t in (("dfinal_states", dfinal_states), ("dinitial_states", dinitial_states)):
+        _expect(name, t, (B, D, W - 1))
+    _expect("dweight", dweight_f32, (D, W))
+    _expect("dbias", dbias_f32, (D,))
     lib = load_library()
     dev = _device_of(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
                      dinitial_states, dweight_f32, dbias_f32)
@@ -210,6 +246,13 @@ def bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinit
 
 
 def update(x, conv_state, weight, bias, cache_seqlens, conv_state_indices, out, silu: bool) -> None:
+    B, D, T, W = _conv_shapes(x, weight, bias, None, None)
+    _expect_dims("conv_state", conv_state, 3)
+    if conv_state.shape[1] != D:
+        raise ValueError(f"conv_state must have dim {D} in its second dimension, got shape {tuple(conv_state.shape)}")
+    _expect("cache_seqlens", cache_seqlens, (B,))
+    _expect("conv_state_indices", conv_state_indices, (B,))
+    _expect("out", out, (B, D, T))
     lib = load_library()
     dev = _device_of(x, conv_state, weight, bias, cache_seqlens, conv_state_indices, out)
     p = UpdateParams(
@@ -222,6 +265,10 @@ def update(x, conv_state, weight, bias, cache_seqlens, conv_state_indices, out, 
 
 
 def varlen_states(x, cu_seqlens, states) -> None:
+    _expect_dims("x", x, 2)
+    _expect_dims("cu_seqlens", cu_seqlens, 1)
+    _expect_dims("states", states, 3)
+    _expect("states", states, (cu_seqlens.shape[0] - 1, x.shape[1], states.shape[2]))
     lib = load_library()
     dev = _device_of(x, cu_seqlens, states)
     p = VarlenParams(states.shape[0], x.shape[1], states.shape[2], x.shape[0],
@@ -231,6 +278,11 @@ def varlen_states(x, cu_seqlens, states) -> None:
 
 
 def fwd_varlen_states(x, weight, bias, seq_idx, cu_seqlens, states, out, silu: bool) -> None:
+    B, D, L, W = _conv_shapes(x, weight, bias, seq_idx, None)
+    _expect("out", out, (B, D, L))
+    _expect_dims("cu_seqlens", cu_seqlens, 1)
+    _expect_dims("states", states, 3)
+    _expect("states", states, (cu_seqlens.shape[0] - 1, D, states.shape[2]))
     lib = load_library()
     dev = _device_of(x, weight, bias, seq_idx, cu_seqlens, states, out)
     f = FwdParams(

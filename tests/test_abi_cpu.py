@@ -68,6 +68,45 @@ def test_validation_errors_need_no_gpu():
     assert lib.cc1d_fwd_varlen_states_launch(ctypes.byref(f), None) == 2
 
 
+def test_shape_errors_before_any_launch():
+    """The launchers check every tensor's shape against the call's (batch, dim, seqlen,
+    width) before touching the device: the C ABI sees only pointers and strides, so a
+    tensor that is too small would otherwise be read or written out of bounds."""
+    import torch
+
+    from causal_conv1d import causal_conv1d_fn
+
+    x = torch.empty(2, 8, 16)
+    w = torch.empty(8, 4)
+    out = torch.empty_like(x)
+    with pytest.raises(ValueError, match="seq_idx"):
+        _abi.fwd(x, w, None, torch.empty(2, 15, dtype=torch.int32), None, None, out, True)
+    with pytest.raises(ValueError, match="seq_idx"):
+        causal_conv1d_fn(x, w, seq_idx=torch.zeros(1, 16, dtype=torch.int32))
+    with pytest.raises(ValueError, match="initial_states"):
+        _abi.fwd(x, w, None, None, torch.empty(2, 8, 2), None, out, True)
+    with pytest.raises(ValueError, match="final_states"):
+        _abi.fwd(x, w, None, None, None, torch.empty(2, 3, 8), out, True)
+    with pytest.raises(ValueError, match="bias"):
+        _abi.fwd(x, w, torch.empty(7), None, None, None, out, True)
+    with pytest.raises(ValueError, match="dout"):
+        _abi.bwd(x, w, None, torch.empty(2, 8, 15), None, None, None, out, None, torch.empty(8, 4), None, True)
+    with pytest.raises(ValueError, match="dfinal_states"):
+        _abi.bwd(x, w, None, out, None, None, torch.empty(2, 8, 4), out, None, torch.empty(8, 4), None, True)
+    x1 = torch.empty(2, 8, 1)
+    with pytest.raises(ValueError, match="conv_state_indices"):
+        _abi.update(x1, torch.empty(2, 8, 3), w, None, None, torch.empty(3, dtype=torch.int32), x1, True)
+    with pytest.raises(ValueError, match="cache_seqlens"):
+        _abi.update(x1, torch.empty(2, 8, 3), w, None, torch.empty(1, dtype=torch.int32), None, x1, True)
+    with pytest.raises(ValueError, match="conv_state"):
+        _abi.update(x1, torch.empty(2, 7, 3), w, None, None, None, x1, True)
+    with pytest.raises(ValueError, match="states"):
+        _abi.varlen_states(torch.empty(20, 8), torch.zeros(4, dtype=torch.int32), torch.empty(2, 8, 3))
+    with pytest.raises(ValueError, match="seq_idx"):
+        _abi.fwd_varlen_states(torch.empty(1, 8, 16), w, None, torch.empty(1, 12, dtype=torch.int32),
+                               torch.zeros(3, dtype=torch.int32), torch.empty(2, 8, 3), torch.empty(1, 8, 16), True)
+
+
 def test_empty_problem_is_a_no_op():
     lib = _abi.load_library()
     p = _abi.FwdParams()
