@@ -653,6 +653,7 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   a.dim = D;
   a.seqlen = T;
   a.state_len = S;
+  a.state_batch = p->state_batch;
   a.x = tensor_arg(p->x);
   a.state = tensor_arg(p->conv_state);
   a.weight = tensor_arg(p->weight);
@@ -710,6 +711,7 @@ static cc1d_status varlen_run(const cc1d_varlen_states_params* p, void* stream) 
   a.batch = B;
   a.dim = D;
   a.state_len = S;
+  a.total_tokens = p->total_tokens;
   a.x = tensor_arg(p->x);
   a.states = tensor_arg(p->states);
   a.cu = p->cu_seqlens.data;

@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
     ok[r] = b < a.batch;
     if (ok[r]) x0[r] = ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1);
     row[r] = (ok[r] && a.indices) ? a.indices[b * a.indices_stride] : static_cast<int>(b);
+    if (row[r] >= a.state_batch) row[r] = -1;  // out of range: a padding row, nothing written
     base[r] = (ok[r] && a.cache_seqlens) ? a.cache_seqlens[b * a.cache_stride] : 0;
   }
 
@@ -211,6 +212,7 @@ __global__ void __launch_bounds__(kThreads) update_shift_kernel(const UpdateArgs
     ok[r] = b < a.batch;
     if (ok[r]) x0[r] = ld_packet<T, CH>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0);
     row[r] = (ok[r] && a.indices) ? a.indices[b * a.indices_stride] : static_cast<int>(b);
+    if (row[r] >= a.state_batch) row[r] = -1;  // out of range: a padding row, nothing written
   }
 #pragma unroll
   for (int r = 0; r < BR; ++r) {
@@ -304,7 +306,7 @@ __global__ void __launch_bounds__(kThreads) varlen_states_kernel(const VarlenArg
     const int64_t token = end - a.state_len + s;
     T* dst = static_cast<T*>(a.states.data) + b * a.states.s0 + cv * VEC * a.states.s1 + s * a.states.s2;
     Packet<T, VEC> v;
-    if (token >= begin) {
+    if (token >= begin && token < a.total_tokens) {  // rows past the end of x give zeros
       v = ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + token * a.x.s0 + cv * VEC * a.x.s1);
     } else {
 #pragma unroll

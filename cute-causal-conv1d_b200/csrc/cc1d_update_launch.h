@@ -11,6 +11,7 @@ constexpr int kUpdateRows = 4;  // batch rows per thread in the update kernel
 
 struct UpdateArgs {
   int64_t batch, dim, seqlen, state_len;
+  int64_t state_batch;  // rows of conv_state: a gather index outside [0, state_batch) is a padding row
   TensorArg x, state, weight, bias, out;
   const int32_t* cache_seqlens;  // nullable
   int64_t cache_stride;
@@ -23,6 +24,7 @@ struct UpdateArgs {
 
 struct VarlenArgs {
   int64_t batch, dim, state_len;
+  int64_t total_tokens;  // rows of x: a gathered row at or past the end gives zeros
   TensorArg x, states;  // x: (tokens, dim) strides s0, s1 ; states: (batch, dim, state_len)
   const void* cu;
   int64_t cu_stride;

@@ -162,7 +162,8 @@ cc1d_status cc1d_bwd_launch_static(const cc1d_bwd_params* params, void* stream);
  *                   history is read at (cache_seqlens[b] - (W-1) + i) mod state_len and
  *                   x[t] is written at (cache_seqlens[b] + t) mod state_len
  *   conv_state_indices (batch,) int32, optional: state row of batch row b; a negative
- *                   index gives a zero output row and no state write
+ *                   index gives a zero output row and no state write, and so does an
+ *                   index >= state_batch (out of range; the reference leaves it undefined)
  * Without cache_seqlens the state becomes the last state_len entries of [state | x].
  * Requires state_len >= width - 1.
  */
@@ -190,7 +191,8 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* params, void* stream);
  *   cu_seqlens  (batch + 1,)              int32 or int64 cumulative sequence offsets
  *   states      (batch, dim, state_len)   output, x's dtype:
  *               states[b, :, s] = x[cu[b+1] - state_len + s] if that row is >= cu[b],
- *               else 0 (bit-exact copy).
+ *               else 0 (bit-exact copy); a row at or past total_tokens gives 0 as well
+ *               (cu_seqlens out of range; the reference leaves it undefined).
  */
 typedef struct cc1d_varlen_states_params {
   int64_t batch, dim, state_len, total_tokens;

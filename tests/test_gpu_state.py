@@ -118,6 +118,42 @@ def test_update_shift_contiguous_state_strided_weight():
     assert np.array_equal(to_storage(sg), es)
 
 
+@pytest.mark.parametrize("state_len", [3, 6])
+@pytest.mark.parametrize("circular", [False, True])
+@pytest.mark.parametrize("channel_last", [True, False])
+def test_update_out_of_range_index_is_a_padding_row(state_len, circular, channel_last):
+    """A conv_state_indices entry >= the number of state rows (undefined in the
+    reference) writes nothing and gives a zero output row, like a negative index."""
+    gen = torch.Generator().manual_seed(21)
+    B, D, W, rows = 4, 256, 4, 5
+    x = torch.randn(B, D, 1, generator=gen).to(torch.bfloat16)
+    state = torch.randn(rows, D, state_len, generator=gen).to(torch.bfloat16)
+    w = torch.rand(D, W, generator=gen) - 0.5
+    idx = torch.tensor([0, 7, 3, rows], dtype=torch.int32)
+    cache = torch.tensor([5, 9, 0, 2], dtype=torch.int32) if circular else None
+    as_padding = torch.where(idx >= rows, torch.full_like(idx, -1), idx)
+    eo, es = O.update(to_storage(x), "bfloat16", to_storage(state), w.numpy(), "float32", None, silu=True,
+                      cache_seqlens=None if cache is None else cache.numpy(), conv_state_indices=as_padding.numpy())
+    sg = state_layout(state.cuda(), channel_last)
+    out = causal_conv1d_update(state_layout(x.cuda(), channel_last), sg, w.cuda(), None, activation="silu",
+                               cache_seqlens=None if cache is None else cache.cuda(), conv_state_indices=idx.cuda())
+    assert_close(out, eo, "bfloat16", PARITY["bfloat16"], "out")
+    assert torch.all(out[1] == 0) and torch.all(out[3] == 0)
+    assert np.array_equal(to_storage(sg), es)
+
+
+def test_varlen_states_rows_past_the_end_are_zero():
+    """cu_seqlens pointing past the last row of x (undefined in the reference) gathers
+    zeros for those rows instead of reading outside x."""
+    gen = torch.Generator().manual_seed(22)
+    x = torch.randn(20, 64, generator=gen).to(torch.float16)
+    cu = torch.tensor([0, 5, 18, 30], dtype=torch.int32)
+    padded = torch.cat([x, torch.zeros(10, 64, dtype=x.dtype)])
+    expected = O.varlen_states(to_storage(padded), cu.numpy(), 4)
+    out = causal_conv1d_varlen_states(x.cuda(), cu.cuda(), 4)
+    assert np.array_equal(to_storage(out), expected)
+
+
 @pytest.mark.parametrize("channel_last", [True, False])
 def test_update_squeezed_2d_input(channel_last):
     gen = torch.Generator().manual_seed(3)
