@@ -669,8 +669,13 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 8) {
-#define CC1D_GO(SI, SQ, EM) \
-  return launch_dependent(fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kFwdStreamThreads, EM>, ls.grid, dim3(kFwdStreamThreads), ls.smem, s, a)
+#define CC1D_GO(SI, SQ, EM)                                                                         \
+  do {                                                                                              \
+    const auto kern = fwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepthFwd, kFwdStreamThreads, EM>; \
+    const cudaError_t ea = allow_dynamic_smem(reinterpret_cast<const void*>(kern), ls.smem);       \
+    if (ea != cudaSuccess) return ea;                                                               \
+    return launch_dependent(kern, ls.grid, dim3(kFwdStreamThreads), ls.smem, s, a);                 \
+  } while (0)
       if (ls.emit) {  // packed sequences: seq_idx is present
         if (silu) CC1D_GO(true, true, true); else CC1D_GO(false, true, true);
       }

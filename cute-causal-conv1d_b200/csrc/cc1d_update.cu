@@ -35,7 +35,10 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
   const int T_len = static_cast<int>(a.seqlen);
   const int S = static_cast<int>(a.state_len);
 
-  // phase 1: first inputs and row indices (independent loads, issued first)
+  // phase 1: first inputs and row indices (independent loads, issued first).  A row
+  // index that is negative or not below state_batch is a padding row; it is tested where
+  // the row is used, so that no instruction waits on an index load before the others
+  // are issued.
   int row[BR], base[BR];
   bool ok[BR];
   Packet<T, VEC> hist[BR][W - 1], x0[BR];
@@ -45,10 +48,10 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
     ok[r] = b < a.batch;
     if (ok[r]) x0[r] = ld_packet<T, VEC>(static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1);
     row[r] = (ok[r] && a.indices) ? a.indices[b * a.indices_stride] : static_cast<int>(b);
-    if (row[r] >= a.state_batch) row[r] = -1;  // out of range: a padding row, nothing written
     base[r] = (ok[r] && a.cache_seqlens) ? a.cache_seqlens[b * a.cache_stride] : 0;
   }
 
+  auto live = [&](int r) { return static_cast<unsigned>(row[r]) < static_cast<unsigned>(a.state_batch); };
   float wv[W][VEC], bv[VEC];
   if (a.weight_vec) {  // contiguous fp32 (dim, W): this thread's VEC*W weights are adjacent
     const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.weight.data) + d0 * W);
@@ -85,7 +88,7 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
   // W-1 entries of the row)
 #pragma unroll
   for (int r = 0; r < BR; ++r) {
-    if (!ok[r] || row[r] < 0) continue;
+    if (!ok[r] || !live(r)) continue;
     if (a.cache_seqlens) {
       base[r] %= S;
       if (base[r] < 0) base[r] += S;
@@ -109,7 +112,7 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
     const int64_t b = b0 + r;
     const T* xp = static_cast<const T*>(a.x.data) + b * a.x.s0 + d0 * a.x.s1;
     T* op = static_cast<T*>(a.out.data) + b * a.out.s0 + d0 * a.out.s1;
-    if (row[r] < 0) {  // padded batch row: zero output, state untouched
+    if (!live(r)) {  // padded batch row: zero output, state untouched
       float z[VEC];
 #pragma unroll
       for (int v = 0; v < VEC; ++v) z[v] = 0.f;
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(kThreads) update_kernel(const UpdateArgs a) {
   // phase 3: state writes (raw copies, bit exact)
 #pragma unroll
   for (int r = 0; r < BR; ++r) {
-    if (!ok[r] || row[r] < 0) continue;
+    if (!ok[r] || !live(r)) continue;
     const T* xp = static_cast<const T*>(a.x.data) + (b0 + r) * a.x.s0 + d0 * a.x.s1;
     T* sp = static_cast<T*>(a.state.data) + (int64_t)row[r] * a.state.s0 + d0 * a.state.s1;
     if (a.cache_seqlens) {
