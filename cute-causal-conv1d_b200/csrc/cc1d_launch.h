@@ -15,6 +15,7 @@ constexpr int kLayoutRows = 1;         // stride over seqlen == 1
 constexpr int kLayoutStream = 2;       // channel-last, per-thread cp.async row stream
 constexpr int kStreamDepth = 8;        // backward: rows in flight per thread (ring slots)
 constexpr int kStreamDepthFwd = 16;    // forward: ring slots per thread (15 rows in flight)
+constexpr int kStreamDepthEmit = 8;    // forward that writes varlen states: ring slots per thread
 constexpr int kStreamThreads = 128;    // CTA size of the row-stream kernel
 constexpr int kFwdStreamThreads = 512; // CTA size of the streamed forward (one CTA per SM)
 constexpr int kBwdStreamThreads = 512; // CTA size of the streamed backward (one CTA per SM at 128 registers)
