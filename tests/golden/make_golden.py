@@ -32,7 +32,9 @@ import torch
 import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("REFERENCE_ROOT")
+if not REF_ROOT:
+    sys.exit("set REFERENCE_ROOT to the reference checkout (the directory holding causal_conv1d/)")
 sys.path.insert(0, REF_ROOT)
 
 from causal_conv1d.causal_conv1d_interface import (  # noqa: E402

@@ -96,8 +96,8 @@ def test_update_grid(dim, width, seqlen, dt, circular, mode):
 @pytest.mark.parametrize("dt", ["float32", "float16", "bfloat16"])
 @pytest.mark.parametrize("mode", ["plain", "gather", "padding"])
 def test_update_shift_contiguous_state(dim, width, seqlen, dt, mode):
-    """(batch, dim, W-1) state with contiguous entries and no circular buffer (config 3a
-    as BASELINE.json gives it): whole channel blocks of the history per thread, bit-exact
+    """(batch, dim, W-1) state with contiguous entries and no circular buffer (config 3a's
+    benchmark layout): whole channel blocks of the history per thread, bit-exact
     state.  dim 2050 is not a whole number of 8-byte channel blocks for 16-bit types and
     takes the per-channel kernel."""
     gen = torch.Generator().manual_seed(dim + 7 * width + seqlen)
