@@ -216,7 +216,9 @@ cc1d_status cc1d_varlen_states_launch(const cc1d_varlen_states_params* params, v
  * is read once and no second launch is made.  Other arguments take the two launches.
  *   fwd         forward params; fwd.batch must be 1 (sequences packed along seqlen)
  *   nseq        number of sequences
- *   cu_seqlens  (nseq + 1,) int32 or int64, non-decreasing, cu[nseq] <= seqlen
+ *   cu_seqlens  (nseq + 1,) int32 or int64, non-decreasing, cu[nseq] <= seqlen (for
+ *               other offsets the states of the sequences concerned are unspecified, but
+ *               nothing outside the given tensors is read or written)
  *   states      (nseq, dim, state_len) output, x's dtype:
  *               states[k, :, s] = x[0, :, cu[k+1] - state_len + s] if that position is
  *               >= cu[k], else 0 (bit-exact copy)
