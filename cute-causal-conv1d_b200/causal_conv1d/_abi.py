@@ -214,8 +214,8 @@ def fwd(x, weight, bias, seq_idx, initial_states, final_states, out, silu: bool)
         _check(lib.cc1d_fwd_launch(ctypes.byref(p), stream))
 
 
-def bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial_states,
-        dweight_f32, dbias_f32, silu: bool, workspace: torch.Tensor | None = None) -> None:
+def _bwd_params(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial_states,
+                dweight_f32, dbias_f32, silu: bool):
     B, D, L, W = _conv_shapes(x, weight, bias, seq_idx, initial_states)
     for name, t in (("dout", dout), ("dx", dx)):
         _expect(name, t, (B, D, L))
@@ -223,7 +223,6 @@ def bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinit
         _expect(name, t, (B, D, W - 1))
     _expect("dweight", dweight_f32, (D, W))
     _expect("dbias", dbias_f32, (D,))
-    lib = load_library()
     dev = _device_of(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
                      dinitial_states, dweight_f32, dbias_f32)
     p = BwdParams(
@@ -233,6 +232,27 @@ def bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinit
         dweight_f32.data_ptr(), dbias_f32.data_ptr() if dbias_f32 is not None else None,
         None, 0, int(bool(silu)), 0,
     )
+    return p, dev
+
+
+def bwd_workspace_bytes(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
+                        dinitial_states, dweight_f32, dbias_f32, silu: bool) -> int:
+    """Device scratch bytes ``bwd`` needs for these arguments (``cc1d_bwd_workspace_bytes``),
+    so that a caller can allocate it once and pass it to every call."""
+    p, _ = _bwd_params(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
+                       dinitial_states, dweight_f32, dbias_f32, silu)
+    lib = load_library()
+    need = lib.cc1d_bwd_workspace_bytes(ctypes.byref(p))
+    if need < 0:
+        _check(lib.cc1d_bwd_launch(ctypes.byref(p), None))  # raises with the message
+    return int(need)
+
+
+def bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial_states,
+        dweight_f32, dbias_f32, silu: bool, workspace: torch.Tensor | None = None) -> None:
+    p, dev = _bwd_params(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
+                         dinitial_states, dweight_f32, dbias_f32, silu)
+    lib = load_library()
     need = lib.cc1d_bwd_workspace_bytes(ctypes.byref(p))
     if need < 0:
         _check(lib.cc1d_bwd_launch(ctypes.byref(p), None))  # raises with the message

@@ -32,7 +32,7 @@ def causal_conv1d_fn_varlen_states(x: Tensor, weight: Tensor, cu_seqlens: Tensor
                                    activation: str | None = None) -> tuple[Tensor, Tensor]:
     """Prefill forward of packed sequences that also returns their decode states.
 
-    Same results as the two calls
+    For offsets that satisfy the precondition below, same results as the two calls
     ``out = causal_conv1d_fn(x, weight, bias, seq_idx=seq_idx, activation=activation)`` and
     ``states = causal_conv1d_varlen_states(x[0].transpose(0, 1), cu_seqlens, state_len)``
     (``causal_conv1d/causal_conv1d_interface.py:99-129`` and
@@ -43,8 +43,10 @@ def causal_conv1d_fn_varlen_states(x: Tensor, weight: Tensor, cu_seqlens: Tensor
     take the two launches.
 
     x: (1, dim, total_tokens), sequences packed along the last dimension;
-    cu_seqlens: (nseq + 1,) int32 or int64 offsets into total_tokens (non-decreasing,
-    last entry <= total_tokens); seq_idx: (1, total_tokens) int32 sequence ids.
+    cu_seqlens: (nseq + 1,) int32 or int64 offsets into total_tokens, non-decreasing with
+    the last entry <= total_tokens (precondition: for other offsets the states of the
+    sequences concerned are unspecified, though nothing outside the given tensors is read
+    or written); seq_idx: (1, total_tokens) int32 sequence ids.
     Returns ``(out, states)``: out like x, states (nseq, dim, state_len) whose memory is
     (nseq, state_len, dim).  An inference call: neither result has autograd history.
     """

@@ -33,6 +33,7 @@ NVCC_FLAGS = ARCH + [
 UNITS = [
     ("cc1d_abi.cu", [], "cc1d_abi.o"),
     ("cc1d_update.cu", [], "cc1d_update.o"),
+    ("cc1d_decode.cu", [], "cc1d_decode.o"),
     ("cc1d_static.cu", [], "cc1d_static.o"),
 ] + [
     (src, [f"-DCC1D_DT={dt}"], f"{src[:-3]}_{name}.o")

@@ -629,6 +629,59 @@ cc1d_status cc1d_update_launch(const cc1d_update_params* p, void* stream) {
   if (B == 0 || D == 0 || T == 0) return CC1D_OK;
   if (!p->x.data || !p->conv_state.data || !p->weight.data || !p->out.data)
     return fail(CC1D_ERR_VALUE, "x, conv_state, weight and out are required");
+  const bool w_flat16 = p->weight.dtype == CC1D_FLOAT32 && p->weight.stride[1] == 1 && p->weight.stride[0] == W &&
+                        aligned16(p->weight.data);
+  const bool b_flat16 = p->bias.data && p->bias.dtype == CC1D_FLOAT32 && p->bias.stride[0] == 1 && aligned16(p->bias.data);
+  // Single-token decode (seqlen == 1) with channel packets in x/out and a state layout one
+  // of the decode kernels takes: every load of a row is issued before any is used.
+  if (T == 1 && B * D <= kMax32) {
+    const cc1d_tensor& st = p->conv_state;
+    const bool circ = p->cache_seqlens.data != nullptr;
+    const int es = elem_size(p->x.dtype);
+    auto ch_ok = [&](const cc1d_tensor& t, int64_t rows, int ch) {
+      return t.stride[1] == 1 && (reinterpret_cast<uintptr_t>(t.data) % (uintptr_t)(ch * es)) == 0 &&
+             stride_ok(t.stride[0], rows, ch) && D % ch == 0;
+    };
+    int kind = -1;
+    const int v16 = 16 / es;
+    if (ch_ok(p->x, B, v16) && ch_ok(p->out, B, v16)) {
+      if (ch_ok(st, p->state_batch, v16) && stride_ok(st.stride[2], S, v16) && (circ || S == W - 1))
+        kind = circ ? kDecodeClCirc : kDecodeClShift;
+      else if (!circ && S == W - 1 && st.stride[2] == 1 && st.stride[1] == S && aligned16(st.data) &&
+               stride_ok(st.stride[0], p->state_batch, v16))
+        kind = kDecodeBlock;
+    }
+    if (kind < 0 && circ && es == 2 && S % 4 == 0 && st.stride[2] == 1 && st.stride[1] == S &&
+        (reinterpret_cast<uintptr_t>(st.data) & 7u) == 0 && stride_ok(st.stride[0], p->state_batch, 4)) {
+      const int ch = decode_channels_per_thread(kDecodeRing, p->x.dtype);
+      if (ch_ok(p->x, B, ch) && ch_ok(p->out, B, ch)) kind = kDecodeRing;
+    }
+    if (kind >= 0) {
+      UpdateArgs a;
+      std::memset(&a, 0, sizeof(a));
+      a.batch = B;
+      a.dim = D;
+      a.seqlen = T;
+      a.state_len = S;
+      a.state_batch = p->state_batch;
+      a.x = tensor_arg(p->x);
+      a.state = tensor_arg(p->conv_state);
+      a.weight = tensor_arg(p->weight);
+      a.bias = tensor_arg(p->bias);
+      a.out = tensor_arg(p->out);
+      a.cache_seqlens = static_cast<const int32_t*>(p->cache_seqlens.data);
+      a.cache_stride = p->cache_seqlens.stride[0];
+      a.indices = static_cast<const int32_t*>(p->conv_state_indices.data);
+      a.indices_stride = p->conv_state_indices.stride[0];
+      a.silu = p->silu;
+      a.weight_vec = w_flat16;
+      a.bias_vec = b_flat16;
+      cudaError_t e = launch_decode(p->x.dtype, kind, a, (int)W, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "causal_conv1d update launch");
+      g_launches.fetch_add(1);
+      return CC1D_OK;
+    }
+  }
   // A shift update (no circular buffer, state_len == W-1) of a state whose entries per
   // channel are contiguous and channels state_len apart: whole 8-byte blocks of
   // channels' histories (update_shift_kernel).
@@ -762,8 +815,9 @@ cc1d_status cc1d_fwd_varlen_states_launch(const cc1d_fwd_varlen_states_params* p
   // variant, the sequence positions fit its 32-bit row counters and the states take
   // its 8-byte packets; otherwise the gather runs as its own launch after the forward.
   const int vec = 8 / elem_size(f.x.dtype);
+  // (seqlen < 2^31 - 1: the kernel clamps offsets to seqlen + 1 in 32-bit arithmetic)
   const bool fused = !no_fwd && !no_states && g.ls.layout == kLayoutStream && f.seq_idx.data &&
-                     p->nseq <= kMax32 && p->state_len <= kMax32 && p->states.stride[1] == 1 &&
+                     f.seqlen < kMax32 && p->nseq <= kMax32 && p->state_len <= kMax32 && p->states.stride[1] == 1 &&
                      (reinterpret_cast<uintptr_t>(p->states.data) & 7u) == 0 &&
                      stride_ok(p->states.stride[0], p->nseq, vec) && stride_ok(p->states.stride[2], p->state_len, vec);
   if (fused) {

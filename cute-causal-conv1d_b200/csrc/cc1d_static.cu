@@ -14,6 +14,8 @@
 // the variable's name as a device address, so the address is looked up once per device
 // with cudaGetSymbolAddress (on the first call on that device, which should therefore
 // happen before any stream capture) and passed to the kernels like a caller workspace.
+// The looked-up address is kept for the life of the process, so the entry point must not
+// be used across a device reset (cudaDeviceReset), which can move the array.
 // All calls share the array: two calls that overlap on the GPU (different streams, or
 // the same array used from several threads without ordering) race on it.
 #include <cstdio>

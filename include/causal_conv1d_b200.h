@@ -147,6 +147,9 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* params, void* stream);
  *     is rejected with CC1D_ERR_VALUE before anything is launched.
  */
 #define CC1D_STATIC_SCRATCH_BYTES (32 * 1024 * 1024)
+/* The device address of the array is looked up once per device and kept for the life of
+ * the process: do not use this entry point across a device reset (cudaDeviceReset) in the
+ * same process. */
 
 cc1d_status cc1d_bwd_launch_static(const cc1d_bwd_params* params, void* stream);
 

@@ -325,3 +325,38 @@ def test_contiguous_states_through_functions(dt, seqlen, width):
     assert_close(dw, edw, "float32", GRAD_PARAM["float32"], "dweight")
     assert_close(db, edb, "float32", GRAD_PARAM["float32"], "dbias")
     assert_close(di, edi, dt, PARITY[dt], "dinitial")
+
+
+@pytest.mark.parametrize("dt", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("width", [2, 3, 4])
+@pytest.mark.parametrize("states", [False, True])
+def test_dx_into_slice_of_wider_gradient_buffer(dt, width, states):
+    """Producer/consumer fusion: x is the channel slice [..., 64:64+D] of a wider
+    (B, L, D+96) projection (reference tests/test_causal_conv1d.py:84-88) and the backward
+    writes dx straight into the same slice of a (B, L, D+96) gradient buffer
+    (reference causal_conv1d_interface.py:72-74).  dx matches the oracle and the columns
+    outside the slice are left untouched."""
+    gen = torch.Generator().manual_seed(31 * width + states + len(dt))
+    B, D, L, W = 2, 136, 515, width
+    tdt = TORCH_DT[dt]
+    x, w, b, init, dout, dfinal = make_inputs(gen, B, D, L, W, dt, True, states, states)
+    wide_x = torch.randn(B, L, D + 96, generator=gen).to(tdt).cuda()
+    wide_x[:, :, 64:64 + D] = x.transpose(1, 2).cuda()
+    xg = wide_x[:, :, 64:64 + D].transpose(1, 2)
+    grad_buf = torch.full((B, L, D + 96), 3.0, dtype=tdt, device="cuda")
+    dxg = grad_buf[:, :, 64:64 + D].transpose(1, 2)
+    init_g = None if init is None else init.cuda()
+    dfinal_g = None if dfinal is None else dfinal.cuda()
+    ret = causal_conv1d_bwd_function(xg, w.cuda(), b.cuda(), with_layout(dout.cuda(), "channel_last"), None, init_g,
+                                     dfinal_g, dxg, states, True)
+    assert ret[0] is dxg
+    edx, edw, edb, edi = O.bwd(to_storage(x), dt, to_storage(w), "float32", to_storage(dout), to_storage(b),
+                               "float32", initial_states=to_storage(init), dfinal_states=to_storage(dfinal),
+                               silu=True)
+    assert_close(dxg, edx, dt, PARITY[dt], "dx in the slice")
+    assert_close(ret[1], edw, "float32", GRAD_PARAM["float32"], "dweight")
+    assert_close(ret[2], edb, "float32", GRAD_PARAM["float32"], "dbias")
+    if states:
+        assert_close(ret[3], edi, dt, PARITY[dt], "dinitial")
+    outside = torch.cat([grad_buf[:, :, :64], grad_buf[:, :, 64 + D:]], dim=2)
+    assert torch.all(outside == 3.0), "columns outside the slice must not be written"

@@ -46,22 +46,24 @@ def test_golden_update(case, channel_last):
 
 
 def run_update_vs_oracle(gen, batch, dim, seqlen, width, state_len, dt, circular, mode, channel_last,
-                         silu=True, squeeze=False):
+                         silu=True, squeeze=False, cache_low=0):
     tdt = TORCH_DT[dt]
     total = batch if mode == "plain" else 3 * batch
     x = torch.randn(batch, dim, seqlen, generator=gen).to(tdt)
     state = torch.randn(total, dim, state_len, generator=gen).to(tdt)
     w = torch.rand(dim, width, generator=gen) - 0.5
     b = torch.randn(dim, generator=gen) * 0.1
-    cache = torch.randint(0, 1000, (batch,), generator=gen, dtype=torch.int32) if circular else None
+    cache = torch.randint(cache_low, 1000, (batch,), generator=gen, dtype=torch.int32) if circular else None
     idx = None
     if mode != "plain":
         idx = torch.randperm(total, generator=gen)[:batch].to(torch.int32)
         if mode == "padding":
             idx[torch.randperm(batch, generator=gen)[: batch // 2]] = -1
+            idx[batch // 2] = total  # out of range: also a padding row
+    # the oracle takes negative indices as padding rows; out-of-range ones are padding too
+    idx_oracle = None if idx is None else np.where(idx.numpy() >= total, -1, idx.numpy())
     eo, es = O.update(to_storage(x), dt, to_storage(state), w.numpy(), "float32", b.numpy(), silu=silu,
-                      cache_seqlens=None if cache is None else cache.numpy(),
-                      conv_state_indices=None if idx is None else idx.numpy())
+                      cache_seqlens=None if cache is None else cache.numpy(), conv_state_indices=idx_oracle)
     xg = state_layout(x.cuda(), channel_last)
     sg = state_layout(state.cuda(), channel_last)
     if squeeze:
@@ -88,6 +90,41 @@ def test_update_grid(dim, width, seqlen, dt, circular, mode):
     state_len = int(torch.randint(width - 1, width + 10, (1,), generator=gen))
     channel_last = (dim + seqlen + width) % 2 == 0
     run_update_vs_oracle(gen, 64, dim, seqlen, width, state_len, dt, circular, mode, channel_last)
+
+
+@pytest.mark.parametrize("dt", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("width", [2, 3, 4])
+@pytest.mark.parametrize("state_len", ["w-1", 6, 8, 16])
+@pytest.mark.parametrize("circular", [False, True])
+@pytest.mark.parametrize("mode", ["plain", "gather", "padding"])
+@pytest.mark.parametrize("channel_last", [True, False])
+def test_update_single_token(dt, width, state_len, circular, mode, channel_last):
+    """seqlen == 1 (the decode step) in every state layout the single-token kernels take:
+    channel-last shift and circular, (B, D, W-1) blocks, (B, D, S) circular rings with
+    S % 4 == 0 (16-bit), and the layouts that fall back to the general kernel (S = 6
+    contiguous, fp32 rings, linear with S > W-1).  Batch 37 leaves a partial row tile;
+    cache_seqlens include negative values (non-negative modulo, as the oracle)."""
+    S = width - 1 if state_len == "w-1" else state_len
+    gen = torch.Generator().manual_seed(100 * width + 7 * S + 3 * circular + len(mode) + channel_last)
+    run_update_vs_oracle(gen, 37, 1040, 1, width, S, dt, circular, mode, channel_last, cache_low=-40)
+
+
+def test_update_single_token_unaligned_views():
+    """x, out and state views whose channel packets are not 16-byte aligned take the
+    general kernel; results are the same."""
+    gen = torch.Generator().manual_seed(31)
+    for channel_last in (True, False):
+        B, D, W, S = 9, 520, 4, 16
+        x = torch.randn(B, D + 1, 1, generator=gen).to(torch.bfloat16)[:, 1:]
+        state = torch.randn(B, D, S, generator=gen).to(torch.bfloat16)
+        w = torch.rand(D, W, generator=gen) - 0.5
+        cache = torch.randint(-5, 100, (B,), generator=gen, dtype=torch.int32)
+        eo, es = O.update(to_storage(x.contiguous()), "bfloat16", to_storage(state), w.numpy(), "float32", None,
+                          silu=True, cache_seqlens=cache.numpy())
+        sg = state_layout(state.cuda(), channel_last)
+        out = causal_conv1d_update(x.cuda(), sg, w.cuda(), None, activation="silu", cache_seqlens=cache.cuda())
+        assert_close(out, eo, "bfloat16", PARITY["bfloat16"], "out")
+        assert np.array_equal(to_storage(sg), es)
 
 
 @pytest.mark.parametrize("dim", [2048, 2052, 2050])

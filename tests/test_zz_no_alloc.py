@@ -123,3 +123,29 @@ def test_static_rejects_problems_beyond_the_array():
     assert "static array" in msg and str(need) in msg and str(limit) in msg
     assert lib.cc1d_launch_count() == before  # nothing was launched
     assert torch.isnan(dx).all()
+
+
+def test_static_entry_allocates_nothing():
+    """The property the entry point exists for: after its first call on the device (which
+    may load the library's device code, the static array included), further calls leave
+    the device's free memory and the PyTorch allocator unchanged."""
+    g = torch.Generator(device="cuda").manual_seed(77)
+    B, D, L, W = 2, 512, 600, 4
+    x = with_layout(torch.randn(B, D, L, generator=g, device="cuda").to(torch.bfloat16), "channel_last")
+    dout = with_layout(torch.randn(B, D, L, generator=g, device="cuda").to(torch.bfloat16), "channel_last")
+    w = torch.rand(D, W, generator=g, device="cuda") - 0.5
+    b = torch.randn(D, generator=g, device="cuda") * 0.1
+    lib = _abi.load_library()
+    dx, dw, db, _ = _outputs(x, w, b, None)
+    p = _params(x, w, b, dout, None, None, None, dx, None, dw, db, True)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.cc1d_bwd_launch_static(ctypes.byref(p), stream) == 0, lib.cc1d_last_error().decode()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    torch0 = torch.cuda.memory_reserved()
+    for _ in range(3):
+        assert lib.cc1d_bwd_launch_static(ctypes.byref(p), stream) == 0, lib.cc1d_last_error().decode()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    assert torch.cuda.memory_reserved() == torch0
