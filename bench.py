@@ -13,9 +13,9 @@ total problem is fixed).  Metric: algorithmic HBM GB/s (every tensor element rea
 written once), summed over ranks, over the max-over-ranks device time.  Every tensor is
 larger than L2 (2 GiB / N >= 256 MiB each), so nothing is re-read from L2 across steps.
 
-Timing: the K timed steps are one CUDA graph holding exactly K steps, replayed once
-between CUDA events (W warm-up steps replay a one-step graph before it).  Per-pass device
-times come from graphs of back-to-back launches of each pass.
+Timing: each of the K timed steps replays a CUDA graph of the forward and one of the
+backward, with a CUDA event after each pass, after W warm-up steps; the step total and each
+pass's average duration (the roofline's "achieved") come from those events.
 
 Per-N figures printed beside the headline: the batch-sharded backward (each rank B/N
 batch rows of all channels) with its NCCL all-reduce of dweight|dbias, as kernel time,
@@ -404,7 +404,8 @@ def cl_randn(shape_bdl, dtype, gen, dev):
 
 # ------------------------------------------------------------------ our arm
 def headline(args, dev, world, rank, sampler_index):
-    """Config-5 forward+backward on this rank's channel shard; K steps in one graph."""
+    """Config-5 forward+backward on this rank's channel shard: K steps, each a replay of a
+    one-launch forward graph and of a backward graph."""
     import torch
     import torch.distributed as dist
 
@@ -432,40 +433,43 @@ def headline(args, dev, world, rank, sampler_index):
     def bwd():
         _abi.bwd(x, w, b, dout, None, None, None, dx, None, dw, db, True, workspace=ws)
 
-    def step():
-        fwd()
-        bwd()
-
-    step()
+    fwd()
+    bwd()
     torch.cuda.synchronize()
-    g1 = capture([step])
     n0 = _abi.launch_count()
-    gk = capture([step] * args.steps)
-    launches = _abi.launch_count() - n0  # kernels in the timed graph
+    g_fwd = capture([fwd])
+    g_bwd = capture([bwd])
+    launches = (_abi.launch_count() - n0) * args.steps  # kernels of the K timed steps
     for _ in range(args.warmup):
-        g1.replay()
+        g_fwd.replay()
+        g_bwd.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The K timed steps replay the forward and backward graphs in turn, with an event
+    # after each pass: the events give the step total and each pass's own duration inside
+    # the timed region (the roofline's "achieved").
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
     sampler = ClockSampler(sampler_index)
     with sampler:
-        t0.record()
-        gk.replay()
-        t1.record()
+        ev[0].record()
+        for i in range(args.steps):
+            g_fwd.replay()
+            ev[2 * i + 1].record()
+            g_bwd.replay()
+            ev[2 * i + 2].record()
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    total_ms = t0.elapsed_time(t1)
-    # per-pass device times: 4 back-to-back launches of each pass in one graph, 3 replays
-    fwd_us = replay_ms(capture([fwd] * 4), 3) / 4 * 1e3
-    bwd_us = replay_ms(capture([bwd] * 4), 3) / 4 * 1e3
+    total_ms = ev[0].elapsed_time(ev[-1])
+    fwd_us = statistics.mean(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) * 1e3
+    bwd_us = statistics.mean(ev[2 * i + 1].elapsed_time(ev[2 * i + 2]) for i in range(args.steps)) * 1e3
     total_ms, fwd_us, bwd_us = rank_max([total_ms, fwd_us, bwd_us], world, dev)
     fb, bb = conv_bytes(B, Dr, L, W)
     res = dict(total_ms=total_ms, fwd_us=fwd_us, bwd_us=bwd_us, fwd_bytes=fb, bwd_bytes=bb,
                launches=launches, clocks=sampler.result(), dim_per_rank=Dr)
-    del g1, gk
+    del g_fwd, g_bwd
     return res
 
 
@@ -791,6 +795,16 @@ def kernel_table(dev, peak, args):
     # config 3: decode update, B=128, D=8192, bf16, silu
     res.update(update_sharded(dev, 1, 0, peak))
 
+    # What a plain device copy (torch copy_) of the same number of bytes reaches in the same
+    # graph harness: the floor that launch, first-load latency and drain put under a
+    # kernel moving 2-34 MB (the update and small forward rows above).
+    for mb in (2, 8, 17, 34):
+        n = mb * (1 << 20) // 2  # bytes read = bytes written
+        pairs = [(torch.empty(n, dtype=torch.uint8, device=dev), torch.empty(n, dtype=torch.uint8, device=dev))
+                 for _ in range(max(4, 512 // mb))]
+        res[f"calibration_copy_{mb}MB"] = entry(2 * n, graph_us([lambda a=a, c=c: c.copy_(a) for a, c in pairs]), peak)
+        del pairs
+
     # config 4: varlen states on (65536, 5120) fp16, 32 sequences, state_len 3
     T, Dv, S, nseq = CFG4["tokens"], CFG4["dim"], CFG4["state_len"], CFG4["nseq"]
     xv = torch.randn(T, Dv, generator=gen, device=dev).to(torch.float16)
@@ -1033,6 +1047,11 @@ def run_case(args):
         cache = torch.randint(0, 1000, (Bu,), generator=gen, device=dev, dtype=torch.int32) if circular else None
         idx = torch.randperm(Bu, generator=gen, device=dev).to(torch.int32) if circular else None
         fn = lambda: causal_conv1d_update(x, st, w, b, "silu", cache, idx)  # noqa: E731
+    elif name.startswith("calibration_copy_"):  # e.g. calibration_copy_17MB: read + write that many bytes
+        n = int(name[len("calibration_copy_"):-2]) * (1 << 20) // 2
+        src = torch.empty(n, dtype=torch.uint8, device=dev)
+        dst = torch.empty(n, dtype=torch.uint8, device=dev)
+        fn = lambda: dst.copy_(src)  # noqa: E731
     elif name == "config4_varlen_states":
         T, Dv, S, nseq = CFG4["tokens"], CFG4["dim"], CFG4["state_len"], CFG4["nseq"]
         xv = torch.randn(T, Dv, generator=gen, device=dev).to(torch.float16)

@@ -174,3 +174,31 @@ def test_config5_slice(dt, width, layout):
         assert_close(db[sl], edb, "float32", GRAD_PARAM["float32"], "dbias")
     del x, dout, out, dx
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("shape,width,dt,states,silu", [
+    ((1, 2048, 2048), 3, "float16", False, True),    # reference README forward shape 1
+    ((1, 4096, 2048), 4, "bfloat16", False, True),   # reference README forward shape 2
+    ((2, 4096, 2048), 4, "bfloat16", True, True),
+    ((3, 1000, 777), 2, "float32", True, False),
+    ((2, 2048, 4099), 4, "float16", True, True),
+    ((8, 1024, 8192), 4, "bfloat16", False, True),
+])
+def test_forward_sizes_across_kernel_choices(shape, width, dt, states, silu):
+    """Channel-last forwards from one small layer to a large batch (the streamed kernel's
+    planner cuts them into very different warp units): whole output and final states
+    against the oracle."""
+    B, D, L = shape
+    g = torch.Generator().manual_seed(B * D + L + width)
+    x = torch.randn(B, L, D, generator=g).to(TORCH_DT[dt]).transpose(1, 2)
+    w = torch.rand(D, width, generator=g) - 0.5
+    b = torch.randn(D, generator=g) * 0.1
+    init = torch.randn(B, D, width - 1, generator=g).to(TORCH_DT[dt]) if states else None
+    eo, ef = O.fwd(to_storage(x), dt, w.numpy(), "float32", b.numpy(), initial_states=to_storage(init), silu=silu,
+                   return_final_states=states)
+    xg = x.transpose(1, 2).contiguous().cuda().transpose(1, 2)
+    final = torch.empty(B, width - 1, D, device="cuda", dtype=TORCH_DT[dt]).transpose(1, 2) if states else None
+    out = causal_conv1d_fwd_function(xg, w.cuda(), b.cuda(), None, None if init is None else init.cuda(), final, silu)
+    assert_close(out, eo, dt, PARITY[dt], "out")
+    if states:
+        assert np.array_equal(to_storage(final), ef)
