@@ -709,7 +709,7 @@ def run_ours(args):
         torch.cuda.empty_cache()
     e2e = run_e2e(args, dev, world, rank) if not args.no_e2e else None
     kernels = {}
-    if world == 1 and not args.no_extras:
+    if world == 1 and not args.no_extras and not args.no_kernel_table:
         kernels = kernel_table(dev, peak, args)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1079,6 +1079,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) figure")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's own GPU kernels")
+    ap.add_argument("--no-kernel-table", action="store_true", help="skip the N=1 per-config kernel table")
     ap.add_argument("--case", default=None, help="run one kernel case (see run_case) and exit")
     ap.add_argument("--case-batch", type=int, default=0, help="batch of a config-2/5 case (0: the config's)")
     ap.add_argument("--repeat", type=int, default=3)
