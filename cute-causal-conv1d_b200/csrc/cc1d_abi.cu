@@ -241,6 +241,9 @@ int64_t choose_units(int64_t ncol, int64_t len, int64_t max_seg, int64_t target,
   return units;
 }
 
+#ifndef CC1D_SPREAD_UNITS
+#define CC1D_SPREAD_UNITS 1
+#endif
 // Streamed channel-last kernels: one wave of warps.  A warp column (32 packets of one
 // batch row) is cut into seg_q or seg_q+1 sequence segments so that the number of warp
 // units equals the resident warp capacity and every warp gets the same number of rows
@@ -264,7 +267,10 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   g.a.seg_q = units / ncol;
   g.a.seg_r = units % ncol;
   g.a.units = units;
+  // CTAs: enough for every unit, and at least one per SM when there are that many units
+  // (the kernels hand units to warps round robin over the CTAs)
   g.ntiles = (units + warps_per_block - 1) / warps_per_block;
+  if (CC1D_SPREAD_UNITS) g.ntiles = std::max<int64_t>(g.ntiles, std::min<int64_t>(units, resident_blocks));
   g.ncounters = 0;  // partials are summed by a second kernel
   g.partial_floats = units * 32 * vec * (width + 1);
   g.ls.smem = bwd ? (size_t)kStreamDepth * kBwdStreamThreads * 16 : (size_t)kStreamDepthFwd * kFwdStreamThreads * 8;

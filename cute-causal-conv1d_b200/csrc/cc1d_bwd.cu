@@ -371,7 +371,9 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
   Pk* xring = reinterpret_cast<Pk*>(smem_raw) + threadIdx.x;
   Pk* gring = reinterpret_cast<Pk*>(smem_raw) + P * NT + threadIdx.x;
   const int lane = threadIdx.x & 31;
-  const int64_t unit = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
+  // warps take units round robin over the CTAs, so that fewer units than resident warps
+  // still spread over every SM (the host sizes the grid)
+  const int64_t unit = (int64_t)(threadIdx.x >> 5) * gridDim.x + blockIdx.x;
   if (unit >= a.units) return;  // whole warps only
   const WarpUnit wu = warp_unit(a, unit);
   const int64_t pb = static_cast<unsigned>(wu.col) / static_cast<unsigned>(a.batch);  // packet block
