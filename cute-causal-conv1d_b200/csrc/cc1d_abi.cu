@@ -241,6 +241,12 @@ int64_t choose_units(int64_t ncol, int64_t len, int64_t max_seg, int64_t target,
   return units;
 }
 
+#ifndef CC1D_MIN_ROWS_FWD
+#define CC1D_MIN_ROWS_FWD 16
+#endif
+#ifndef CC1D_MIN_ROWS_BWD
+#define CC1D_MIN_ROWS_BWD 32
+#endif
 #ifndef CC1D_SPREAD_UNITS
 #define CC1D_SPREAD_UNITS 1
 #endif
@@ -258,7 +264,7 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   const int64_t nv = D / vec;
   const int64_t warps_per_block = (bwd ? kBwdStreamThreads : kFwdStreamThreads) / 32;
   const int64_t ncol = B * ((nv + 31) / 32);
-  const int64_t min_rows = bwd ? 32 : 16;
+  const int64_t min_rows = bwd ? CC1D_MIN_ROWS_BWD : CC1D_MIN_ROWS_FWD;  // shortest segment
   const int64_t max_seg = std::max<int64_t>(1, L / min_rows);
   const int64_t target = std::max<int64_t>(1, resident_blocks * warps_per_block);
   const int64_t units = choose_units(ncol, L, max_seg, target, /*unit_overhead=*/24);
