@@ -606,8 +606,8 @@ __global__ void __launch_bounds__(NT) bwd_stream_kernel(const ConvArgs a) {
 // channel), so one unit's slots form a contiguous slab of 32*PER_LANE floats, and the
 // units of packet block pb (all batch rows, all segments) are contiguous.
 // A block owns one value index r of one packet block (32 lanes); each of its
-// kReduceChains warps adds every kReduceChains-th unit in unit order (loads issued four
-// at a time), and warp 0 adds the chains in chain order.  The order of every addition
+// kReduceChains warps adds every kReduceChains-th unit in unit order (loads issued
+// sixteen at a time), and warp 0 adds the chains in chain order.  The order of every addition
 // depends only on the geometry, so the result is reproducible.
 constexpr int kReduceChains = 8;
 
@@ -626,18 +626,17 @@ __global__ void __launch_bounds__(32 * kReduceChains) reduce_unit_partials(const
   const int64_t u0 = first_unit(a, pb * a.batch), u1 = first_unit(a, (pb + 1) * a.batch);
   const float* src = a.partials + q;
   float acc = 0.f;
-  int64_t k = u0 + chain;
-  for (; k + 3 * S < u1; k += 4 * S) {
-    const float v0 = __ldcg(src + (k + 0 * S) * SLAB);
-    const float v1 = __ldcg(src + (k + 1 * S) * SLAB);
-    const float v2 = __ldcg(src + (k + 2 * S) * SLAB);
-    const float v3 = __ldcg(src + (k + 3 * S) * SLAB);
-    acc += v0;
-    acc += v1;
-    acc += v2;
-    acc += v3;
+  // up to 16 units per chain are loaded at once (one L2 round trip for up to 128 units
+  // per packet block), then added in unit order
+  constexpr int BATCH = 16;
+  for (int64_t k = u0 + chain; k < u1; k += BATCH * S) {
+    float v[BATCH];
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) v[i] = (k + i * S < u1) ? __ldcg(src + (k + i * S) * SLAB) : 0.f;
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i)
+      if (k + i * S < u1) acc += v[i];
   }
-  for (; k < u1; k += S) acc += __ldcg(src + k * SLAB);
   chain_sum[chain][lane] = acc;
   __syncthreads();
   if (chain != 0) return;
