@@ -111,17 +111,20 @@ class ClockSampler:
             self.handle = None
         self.thread = threading.Thread(target=self._run, daemon=True)
 
+    def _sample(self):
+        try:
+            self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+            self.reasons |= int(self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+        except Exception:
+            pass
+
     def _run(self):
-        while not self._stop.is_set():
-            try:
-                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
-                self.reasons |= int(self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
-            except Exception:
-                pass
-            time.sleep(self.period)
+        while not self._stop.wait(self.period):
+            self._sample()
 
     def __enter__(self):
         if self.handle is not None:
+            self._sample()  # one sample as the region starts, then one per period
             self.thread.start()
         return self
 
@@ -129,6 +132,7 @@ class ClockSampler:
         self._stop.set()
         if self.handle is not None:
             self.thread.join()
+            self._sample()  # and one as it ends (before the host synchronises)
         return False
 
     def result(self):
@@ -479,6 +483,7 @@ def batch_sharded_bwd(args, dev, world, rank):
     all-reduce time and the overlapped step (the all-reduce of step i on a side stream
     under the backward of step i+1, two buckets) are timed separately."""
     import torch
+    import torch.distributed as dist
 
     from causal_conv1d import _abi
     from causal_conv1d.distributed import GradBucket, allreduce_param_grads, shard_range
@@ -510,11 +515,25 @@ def batch_sharded_bwd(args, dev, world, rank):
         with torch.cuda.stream(side):
             allreduce_param_grads(buckets[1])
     torch.cuda.synchronize()
-    kern_us = replay_ms(capture([lambda k=i % 2: bwd(k) for i in range(K)]), 2) / K * 1e3
+
+    def settle():  # every rank starts each timed replay together
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    g_kern = capture([lambda k=i % 2: bwd(k) for i in range(K)])
+    settle()
+    kern_us = replay_ms(g_kern, 2) / K * 1e3
+    del g_kern
     ar_us = 0.0
     step_us = kern_us
     if world > 1:
-        ar_us = replay_ms(capture([lambda k=i % 2: allreduce_param_grads(buckets[k]) for i in range(K)]), 2) / K * 1e3
+        g_ar = capture([lambda k=i % 2: allreduce_param_grads(buckets[k]) for i in range(K)])
+        g_ar.replay()
+        settle()
+        ar_us = replay_ms(g_ar, 2) / K * 1e3
+        del g_ar
         done = [torch.cuda.Event() for _ in range(2)]
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
@@ -530,7 +549,7 @@ def batch_sharded_bwd(args, dev, world, rank):
                     done[k].record(side)
             cap.wait_stream(side)
         g.replay()
-        torch.cuda.synchronize()
+        settle()
         step_us = replay_ms(g, 2) / K * 1e3
         del g
     kern_us, ar_us, step_us = rank_max([kern_us, ar_us, step_us], world, dev)
