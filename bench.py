@@ -1066,6 +1066,19 @@ def run_case(args):
         cache = torch.randint(0, 1000, (Bu,), generator=gen, device=dev, dtype=torch.int32) if circular else None
         idx = torch.randperm(Bu, generator=gen, device=dev).to(torch.int32) if circular else None
         fn = lambda: causal_conv1d_update(x, st, w, b, "silu", cache, idx)  # noqa: E731
+    elif name.startswith("readme_") or name.startswith("ref_readme_"):
+        # the reference README's forward shapes; ref_* runs the reference's own CuTe DSL kernel
+        shape, W_, dt = ((1, 2048, 2048), 3, torch.float16) if "fp16" in name else ((1, 4096, 2048), 4, torch.bfloat16)
+        x = cl_randn(shape, dt, gen, dev)
+        w = torch.rand(shape[1], W_, generator=gen, device=dev) - 0.5
+        b = torch.randn(shape[1], generator=gen, device=dev) * 0.1
+        if name.startswith("ref_"):
+            K, why = _load_reference_kernels()
+            if K is None:
+                raise SystemExit(why)
+            fn = lambda: K.causal_conv1d_fwd_cutedsl(x, w, b, "silu")  # noqa: E731
+        else:
+            fn = lambda: causal_conv1d_fwd_function(x, w, b, None, None, None, True)  # noqa: E731
     elif name.startswith("calibration_copy_"):  # e.g. calibration_copy_17MB: read + write that many bytes
         n = int(name[len("calibration_copy_"):-2]) * (1 << 20) // 2
         src = torch.empty(n, dtype=torch.uint8, device=dev)

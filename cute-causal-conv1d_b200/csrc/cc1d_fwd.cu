@@ -671,21 +671,30 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
     if constexpr (VEC * sizeof(T) == 8) {
-#define CC1D_GO(SI, SQ, EM)                                                                         \
+#define CC1D_GO_P(SI, SQ, EM, P, NT)                                                                \
   do {                                                                                              \
-    const auto kern = fwd_stream_kernel<T, W, VEC, SI, SQ, (EM ? kStreamDepthEmit : kStreamDepthFwd), kFwdStreamThreads, EM>; \
+    const auto kern = fwd_stream_kernel<T, W, VEC, SI, SQ, P, NT, EM>;                              \
     const cudaError_t ea = allow_dynamic_smem(reinterpret_cast<const void*>(kern), ls.smem);       \
     if (ea != cudaSuccess) return ea;                                                               \
-    return launch_dependent(kern, ls.grid, dim3(kFwdStreamThreads), ls.smem, s, a);                 \
+    return launch_dependent(kern, ls.grid, dim3(NT), ls.smem, s, a);                                \
   } while (0)
+#define CC1D_GO(SI, SQ, EM)                                                                         \
+  CC1D_GO_P(SI, SQ, EM, (EM ? kStreamDepthEmit : kStreamDepthFwd), kFwdStreamThreads)
+#define CC1D_GO_SMALL(SI, SQ) CC1D_GO_P(SI, SQ, false, kStreamDepthFwdSmall, kFwdStreamThreadsSmall)
       // The state-emitting variant keeps 8-slot rings: with 16-row blocks it ran 362 us
       // instead of 252 us on 1024 packed sequences of 64 rows (config 4's shape).
       if (ls.emit) {  // packed sequences: seq_idx is present
         if (silu) CC1D_GO(true, true, true); else CC1D_GO(false, true, true);
       }
+      if (ls.small) {
+        if (silu) { if (seq) CC1D_GO_SMALL(true, true); else CC1D_GO_SMALL(true, false); }
+        else { if (seq) CC1D_GO_SMALL(false, true); else CC1D_GO_SMALL(false, false); }
+      }
       if (silu) { if (seq) CC1D_GO(true, true, false); else CC1D_GO(true, false, false); }
       else { if (seq) CC1D_GO(false, true, false); else CC1D_GO(false, false, false); }
+#undef CC1D_GO_SMALL
 #undef CC1D_GO
+#undef CC1D_GO_P
     }
   } else if (ls.layout == kLayoutChannelLast) {
     constexpr int U = 4;
@@ -730,6 +739,9 @@ static const void* fwd_kernel_ptr_t(const LaunchShape& ls) {
   // Any instantiation of the same family has the same resource footprint class; the
   // host uses this only for occupancy queries.
   constexpr int PV = 16 / sizeof(T);
+  if (ls.layout == kLayoutStream && ls.small)
+    return reinterpret_cast<const void*>(
+        fwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepthFwdSmall, kFwdStreamThreadsSmall>);
   if (ls.layout == kLayoutStream)
     return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepthFwd, kFwdStreamThreads>);
   if (ls.layout == kLayoutChannelLast) {

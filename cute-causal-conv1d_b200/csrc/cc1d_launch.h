@@ -18,6 +18,8 @@ constexpr int kStreamDepthFwd = 16;    // forward: ring slots per thread (15 row
 constexpr int kStreamDepthEmit = 8;    // forward that writes varlen states: ring slots per thread
 constexpr int kStreamThreads = 128;    // CTA size of the row-stream kernel
 constexpr int kFwdStreamThreads = 512; // CTA size of the streamed forward (one CTA per SM)
+constexpr int kStreamDepthFwdSmall = 8;     // streamed forward of small problems: ring slots
+constexpr int kFwdStreamThreadsSmall = 128; // streamed forward of small problems: CTA size
 constexpr int kBwdStreamThreads = 512; // CTA size of the streamed backward (one CTA per SM at 128 registers)
 constexpr int kLayoutRowStream = 3;    // (batch, dim, seqlen)-contiguous, per-lane sector stream
 constexpr int kRowDepthBwd = 4;        // row-stream backward: ring slots (32-byte sectors) per lane and tensor
@@ -33,6 +35,7 @@ struct LaunchShape {
   bool silu;
   bool seq;
   bool emit;    // streamed forward only: also write the varlen states (ConvArgs::states)
+  bool small;   // streamed forward only: the small-problem configuration (128-thread CTAs, 8-slot rings)
   size_t smem;
 };
 
