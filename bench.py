@@ -50,9 +50,6 @@ CFG5 = dict(batch=8, dim=16384, seqlen=8192, width=4)
 CFG2 = dict(batch=4, dim=4096, seqlen=2048, width=4)
 CFG3 = dict(batch=128, dim=8192, width=4)
 CFG4 = dict(tokens=65536, dim=5120, nseq=32, width=4, state_len=3)
-# SMs the batch-sharded backward leaves free for the all-reduce that overlaps it (the NCCL
-# kernel is held to as many CTAs, NCCL_MAX_CTAS)
-SM_RESERVE = 8
 
 
 def _package_path():
@@ -484,8 +481,7 @@ def batch_sharded_bwd(args, dev, world, rank):
     """Config-5 backward sharded over batch: each rank runs its B/N rows of all channels,
     then one NCCL all-reduce of the flat fp32 dweight|dbias bucket.  Kernel time,
     all-reduce time and the overlapped step (the all-reduce of step i on a side stream
-    under the backward of step i+1, two buckets; that backward leaves SM_RESERVE SMs to the
-    all-reduce) are timed separately."""
+    under the backward of step i+1, two buckets) are timed separately."""
     import torch
     import torch.distributed as dist
 
@@ -503,14 +499,13 @@ def batch_sharded_bwd(args, dev, world, rank):
     w = torch.rand(D, W, generator=pg, device=dev) - 0.5
     b = torch.randn(D, generator=pg, device=dev) * 0.1
     buckets = [GradBucket(D, W, True, dev) for _ in range(2)]
-    need = max(_abi.bwd_workspace_bytes(x, w, b, dout, None, None, None, dx, None,
-                                        buckets[0].dweight, buckets[0].dbias, True, sm_reserve=r)
-               for r in (0, SM_RESERVE))
+    need = _abi.bwd_workspace_bytes(x, w, b, dout, None, None, None, dx, None,
+                                    buckets[0].dweight, buckets[0].dbias, True)
     ws = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
 
-    def bwd(k, reserve=0):
+    def bwd(k):
         _abi.bwd(x, w, b, dout, None, None, None, dx, None, buckets[k].dweight, buckets[k].dbias, True,
-                 workspace=ws, sm_reserve=reserve)
+                 workspace=ws)
 
     K = max(4, args.steps)
     bwd(0)
@@ -547,7 +542,7 @@ def batch_sharded_bwd(args, dev, world, rank):
                 k = i % 2
                 if i >= 2:
                     cap.wait_event(done[k])  # the all-reduce that last read this bucket
-                bwd(k, SM_RESERVE)  # leaves SMs free for the previous step's all-reduce
+                bwd(k)
                 side.wait_stream(cap)
                 with torch.cuda.stream(side):
                     allreduce_param_grads(buckets[k])
@@ -708,7 +703,6 @@ def run_ours(args):
         # the only collective moves 320 KB: NVLink SHARP brings nothing at that size, so it
         # stays off (no multicast memory objects are created)
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        os.environ.setdefault("NCCL_MAX_CTAS", str(SM_RESERVE))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     from causal_conv1d import _abi
 

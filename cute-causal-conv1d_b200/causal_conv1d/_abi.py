@@ -47,7 +47,7 @@ class BwdParams(ctypes.Structure):
         ("initial_states", CTensor), ("dout", CTensor), ("dfinal_states", CTensor),
         ("dx", CTensor), ("dinitial_states", CTensor),
         ("dweight", c_void_p), ("dbias", c_void_p), ("workspace", c_void_p),
-        ("workspace_bytes", c_i64), ("silu", c_i32), ("sm_reserve", c_i32),
+        ("workspace_bytes", c_i64), ("silu", c_i32), ("reserved", c_i32),
     ]
 
 
@@ -215,7 +215,7 @@ def fwd(x, weight, bias, seq_idx, initial_states, final_states, out, silu: bool)
 
 
 def _bwd_params(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial_states,
-                dweight_f32, dbias_f32, silu: bool, sm_reserve: int = 0):
+                dweight_f32, dbias_f32, silu: bool):
     B, D, L, W = _conv_shapes(x, weight, bias, seq_idx, initial_states)
     for name, t in (("dout", dout), ("dx", dx)):
         _expect(name, t, (B, D, L))
@@ -230,17 +230,17 @@ def _bwd_params(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, d
         _ct(x), _ct(weight), _ct(bias), _ct(seq_idx), _ct(initial_states), _ct(dout),
         _ct(dfinal_states), _ct(dx), _ct(dinitial_states),
         dweight_f32.data_ptr(), dbias_f32.data_ptr() if dbias_f32 is not None else None,
-        None, 0, int(bool(silu)), int(sm_reserve),
+        None, 0, int(bool(silu)), 0,
     )
     return p, dev
 
 
 def bwd_workspace_bytes(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
-                        dinitial_states, dweight_f32, dbias_f32, silu: bool, sm_reserve: int = 0) -> int:
+                        dinitial_states, dweight_f32, dbias_f32, silu: bool) -> int:
     """Device scratch bytes ``bwd`` needs for these arguments (``cc1d_bwd_workspace_bytes``),
     so that a caller can allocate it once and pass it to every call."""
     p, _ = _bwd_params(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
-                       dinitial_states, dweight_f32, dbias_f32, silu, sm_reserve)
+                       dinitial_states, dweight_f32, dbias_f32, silu)
     lib = load_library()
     need = lib.cc1d_bwd_workspace_bytes(ctypes.byref(p))
     if need < 0:
@@ -249,12 +249,9 @@ def bwd_workspace_bytes(x, weight, bias, dout, seq_idx, initial_states, dfinal_s
 
 
 def bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial_states,
-        dweight_f32, dbias_f32, silu: bool, workspace: torch.Tensor | None = None, sm_reserve: int = 0) -> None:
-    """Backward launch.  ``sm_reserve`` SMs are left free for work that runs concurrently on
-    another stream (a collective): a kernel that fills every SM would hold it back until
-    the kernel ends."""
+        dweight_f32, dbias_f32, silu: bool, workspace: torch.Tensor | None = None) -> None:
     p, dev = _bwd_params(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx,
-                         dinitial_states, dweight_f32, dbias_f32, silu, sm_reserve)
+                         dinitial_states, dweight_f32, dbias_f32, silu)
     lib = load_library()
     need = lib.cc1d_bwd_workspace_bytes(ctypes.byref(p))
     if need < 0:

@@ -74,15 +74,12 @@ def allreduce_param_grads(bucket: GradBucket, group=None, deterministic: bool = 
 def causal_conv1d_bwd_batch_sharded(x, weight, bias, dout, seq_idx=None, initial_states=None,
                                     dfinal_states=None, silu_activation=False, return_dinitial_states=False,
                                     bucket: GradBucket | None = None, group=None, allreduce=True,
-                                    deterministic: bool = False, sm_reserve: int = 0):
+                                    deterministic: bool = False):
     """Backward of this rank's batch shard, then the dweight/dbias all-reduce.
 
     Returns ``(dx, dweight, dbias, dinitial_states)`` like
     ``cpp_functions.causal_conv1d_bwd_function``; dweight/dbias are the sums over all
-    ranks, in the parameter dtypes.  ``sm_reserve`` leaves that many SMs free for a
-    collective that the caller runs at the same time on another stream (the previous
-    step's all-reduce): the backward otherwise fills every SM and the collective's kernel
-    waits for it.
+    ranks, in the parameter dtypes.
     """
     dim, width = weight.shape
     if bucket is None:
@@ -93,7 +90,7 @@ def causal_conv1d_bwd_batch_sharded(x, weight, bias, dout, seq_idx=None, initial
     if initial_states is not None and return_dinitial_states:
         dinitial = torch.empty_like(initial_states)
     _abi.bwd(x, weight, bias, dout, seq_idx, initial_states, dfinal_states, dx, dinitial,
-             bucket.dweight, bucket.dbias, silu_activation, sm_reserve=sm_reserve)
+             bucket.dweight, bucket.dbias, silu_activation)
     if allreduce:
         allreduce_param_grads(bucket, group, deterministic)
     dw = bucket.dweight if weight.dtype == torch.float32 else bucket.dweight.to(weight.dtype)

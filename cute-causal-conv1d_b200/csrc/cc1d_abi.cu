@@ -507,11 +507,6 @@ cc1d_status cc1d_fwd_launch(const cc1d_fwd_params* p, void* stream) {
   return fwd_run(p, g, stream);
 }
 
-// SMs a backward launch may use: all but the caller's sm_reserve, at least one.
-static int64_t bwd_sms(const cc1d_bwd_params* p) {
-  return std::max<int64_t>(1, (int64_t)sm_count() - std::max<int32_t>(0, p->sm_reserve));
-}
-
 static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* empty) {
   if (!p) return fail(CC1D_ERR_VALUE, "params is NULL");
   cc1d_status st = check_conv_common(p->batch, p->dim, p->seqlen, p->width, p->x, p->weight, p->bias,
@@ -530,17 +525,15 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
   *empty = (B == 0 || D == 0 || L == 0);
   if (*empty) return CC1D_OK;
   if (!p->dout.data || !p->dx.data || !p->dweight) return fail(CC1D_ERR_VALUE, "dout, dx and dweight are required");
-  if (p->sm_reserve < 0) return fail(CC1D_ERR_VALUE, "sm_reserve must be >= 0");
   int layout = kLayoutChannelLast;
   bool packet = false;
   const int es = elem_size(p->x.dtype);
-  const int64_t sms = bwd_sms(p);
   if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->dout, B, D, L, 8) && stream_ok(p->dx, B, D, L, 8)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
     const size_t smem = (size_t)kStreamDepth * kBwdStreamThreads * 16;
     probe.smem = smem;
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kBwdStreamThreads) * sms;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kBwdStreamThreads) * sm_count();
     *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }
@@ -548,7 +541,7 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
     LaunchShape probe{};
     probe.layout = kLayoutRowWalk;
     probe.smem = (size_t)2 * kRowWalkDepth * kRowWalkThreads * 16;
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), probe.smem, kRowWalkThreads) * sms;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), probe.smem, kRowWalkThreads) * sm_count();
     *out_g = plan_rowwalk(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }
@@ -557,7 +550,7 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
     LaunchShape probe{};
     probe.layout = kLayoutRowStream;
     const size_t smem = (size_t)2 * kRowDepthBwd * kStreamThreads * 32;
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kStreamThreads) * sms;
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kStreamThreads) * sm_count();
     *out_g = plan_rows(true, B, D, L, (int)p->width, es, resident);
     return CC1D_OK;
   }
@@ -633,7 +626,7 @@ cc1d_status cc1d_bwd_launch(const cc1d_bwd_params* p, void* stream) {
   if (g.ls.layout == kLayoutStream || g.ls.layout == kLayoutRowStream || g.ls.layout == kLayoutRowWalk) {
     g.ls.grid = dim3((unsigned)g.ntiles);
   } else {
-    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, g.ls), g.ls.smem) * bwd_sms(p);
+    const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, g.ls), g.ls.smem) * sm_count();
     g.ls.grid = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(g.ntiles, resident)));
   }
   e = dispatch(true, p->x.dtype, a, g.ls, s);

@@ -123,9 +123,7 @@ typedef struct cc1d_bwd_params {
   void* workspace;
   int64_t workspace_bytes;
   int32_t silu;
-  int32_t sm_reserve; /* SMs the launch leaves free (0: use every SM), e.g. for a collective
-                         that runs on another stream at the same time: a kernel that fills
-                         every SM would hold it back until the kernel ends */
+  int32_t reserved;
 } cc1d_bwd_params;
 
 /* Scratch bytes cc1d_bwd_launch needs for these params (0 for empty problems), or

@@ -360,33 +360,3 @@ def test_dx_into_slice_of_wider_gradient_buffer(dt, width, states):
         assert_close(ret[3], edi, dt, PARITY[dt], "dinitial")
     outside = torch.cat([grad_buf[:, :, :64], grad_buf[:, :, 64 + D:]], dim=2)
     assert torch.all(outside == 3.0), "columns outside the slice must not be written"
-
-
-@pytest.mark.parametrize("layout", ["channel_last", "contiguous"])
-def test_backward_with_sms_left_free(layout):
-    """sm_reserve (SMs left free for a concurrent collective) changes the launch shape
-    only: results within tolerance of the oracle, reproducible call to call, and a
-    reserve larger than the GPU still leaves one SM."""
-    from causal_conv1d import _abi
-
-    gen = torch.Generator().manual_seed(12)
-    B, D, L, W = 2, 512, 1500, 4
-    x, w, b, _, dout, _ = make_inputs(gen, B, D, L, W, "bfloat16", True, False, False, w_scale=0.5)
-    edx, edw, edb, _ = O.bwd(to_storage(x), "bfloat16", w.numpy(), "float32", to_storage(dout), b.numpy(),
-                             silu=True)
-    xg, gg = with_layout(x.cuda(), layout), with_layout(dout.cuda(), layout)
-    for reserve in (0, 8, 100000):
-        runs = []
-        for _ in range(2):
-            dx = torch.empty_like(xg)
-            dw = torch.empty(D, W, device="cuda")
-            db = torch.empty(D, device="cuda")
-            _abi.bwd(xg, w.cuda(), b.cuda(), gg, None, None, None, dx, None, dw, db, True, sm_reserve=reserve)
-            runs.append((dx, dw, db))
-        assert_close(runs[0][0], edx, "bfloat16", PARITY["bfloat16"], "dx")
-        assert_close(runs[0][1], edw, "float32", GRAD_PARAM["float32"], "dweight")
-        assert_close(runs[0][2], edb, "float32", GRAD_PARAM["float32"], "dbias")
-        assert all(torch.equal(a, c) for a, c in zip(*runs))
-    with pytest.raises(ValueError):
-        _abi.bwd(xg, w.cuda(), b.cuda(), gg, None, None, None, torch.empty_like(xg), None,
-                 torch.empty(D, W, device="cuda"), torch.empty(D, device="cuda"), True, sm_reserve=-1)
