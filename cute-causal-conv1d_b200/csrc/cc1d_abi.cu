@@ -262,7 +262,7 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   g.ls.layout = kLayoutStream;
   g.ls.packet = true;
   g.ls.small = small;
-  const int vec = 8 / es;  // both streamed kernels move 8-byte packets
+  const int vec = (bwd ? kBwdPacketBytes : kFwdPacketBytes) / es;  // bytes of channels per lane and row
   const int64_t nv = D / vec;
   const int64_t warps_per_block = (bwd ? kBwdStreamThreads : small ? kFwdStreamThreadsSmall : kFwdStreamThreads) / 32;
   const int64_t ncol = B * ((nv + 31) / 32);
@@ -281,9 +281,9 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   if (CC1D_SPREAD_UNITS) g.ntiles = std::max<int64_t>(g.ntiles, std::min<int64_t>(units, resident_blocks));
   g.ncounters = 0;  // partials are summed by a second kernel
   g.partial_floats = units * 32 * vec * (width + 1);
-  g.ls.smem = bwd     ? (size_t)kStreamDepth * kBwdStreamThreads * 16
-              : small ? (size_t)kStreamDepthFwdSmall * kFwdStreamThreadsSmall * 8
-                      : (size_t)kStreamDepthFwd * kFwdStreamThreads * 8;
+  g.ls.smem = bwd     ? (size_t)kStreamDepth * kBwdStreamThreads * 2 * kBwdPacketBytes  // x and dout rings
+              : small ? (size_t)kStreamDepthFwdSmall * kFwdStreamThreadsSmall * kFwdPacketBytes
+                      : (size_t)kStreamDepthFwd * kFwdStreamThreads * kFwdPacketBytes;
   return g;
 }
 
@@ -434,7 +434,7 @@ static cc1d_status fwd_prepare(const cc1d_fwd_params* p, Geometry* out_g, bool* 
   bool packet = false;
   const int es = elem_size(p->x.dtype);
   Geometry& g = *out_g;
-  if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->out, B, D, L, 8)) {
+  if (stream_ok(p->x, B, D, L, kFwdPacketBytes) && stream_ok(p->out, B, D, L, kFwdPacketBytes)) {
     // One CTA of 16 warps per SM with a 16-slot ring: measured faster than two CTAs per
     // SM with 8-slot rings (config 2 forward 26.5 -> 25.4 us, config 4 233 -> 228 us),
     // since each warp walks twice the rows for the same start-up.
@@ -448,7 +448,7 @@ static cc1d_status fwd_prepare(const cc1d_fwd_params* p, Geometry* out_g, bool* 
       LaunchShape probe{};
       probe.layout = kLayoutStream;
       probe.small = true;
-      probe.smem = (size_t)kStreamDepthFwdSmall * kFwdStreamThreadsSmall * 8;
+      probe.smem = (size_t)kStreamDepthFwdSmall * kFwdStreamThreadsSmall * kFwdPacketBytes;
       const int64_t resident =
           (int64_t)blocks_per_sm(kernel_ptr(false, p->x.dtype, probe), probe.smem, kFwdStreamThreadsSmall) * sm_count();
       g = plan_stream(false, B, D, L, W, es, resident, true);
@@ -528,10 +528,11 @@ static cc1d_status bwd_prepare(const cc1d_bwd_params* p, Geometry* out_g, bool* 
   int layout = kLayoutChannelLast;
   bool packet = false;
   const int es = elem_size(p->x.dtype);
-  if (stream_ok(p->x, B, D, L, 8) && stream_ok(p->dout, B, D, L, 8) && stream_ok(p->dx, B, D, L, 8)) {
+  if (stream_ok(p->x, B, D, L, kBwdPacketBytes) && stream_ok(p->dout, B, D, L, kBwdPacketBytes) &&
+      stream_ok(p->dx, B, D, L, kBwdPacketBytes)) {
     LaunchShape probe{};
     probe.layout = kLayoutStream;
-    const size_t smem = (size_t)kStreamDepth * kBwdStreamThreads * 16;
+    const size_t smem = (size_t)kStreamDepth * kBwdStreamThreads * 2 * kBwdPacketBytes;
     probe.smem = smem;
     const int64_t resident = (int64_t)blocks_per_sm(kernel_ptr(true, p->x.dtype, probe), smem, kBwdStreamThreads) * sm_count();
     *out_g = plan_stream(true, B, D, L, (int)p->width, es, resident);
@@ -843,12 +844,12 @@ cc1d_status cc1d_fwd_varlen_states_launch(const cc1d_fwd_varlen_states_params* p
   if (st != CC1D_OK) return st;
   // The streamed forward writes the states itself when it runs the packed (seq_idx)
   // variant, the sequence positions fit its 32-bit row counters and the states take
-  // its 8-byte packets; otherwise the gather runs as its own launch after the forward.
-  const int vec = 8 / elem_size(f.x.dtype);
+  // its packets; otherwise the gather runs as its own launch after the forward.
+  const int vec = kFwdPacketBytes / elem_size(f.x.dtype);
   // (seqlen < 2^31 - 1: the kernel clamps offsets to seqlen + 1 in 32-bit arithmetic)
   const bool fused = !no_fwd && !no_states && g.ls.layout == kLayoutStream && f.seq_idx.data &&
                      f.seqlen < kMax32 && p->nseq <= kMax32 && p->state_len <= kMax32 && p->states.stride[1] == 1 &&
-                     (reinterpret_cast<uintptr_t>(p->states.data) & 7u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p->states.data) % kFwdPacketBytes) == 0 &&
                      stride_ok(p->states.stride[0], p->nseq, vec) && stride_ok(p->states.stride[2], p->state_len, vec);
   if (fused) {
     ConvArgs& a = g.a;

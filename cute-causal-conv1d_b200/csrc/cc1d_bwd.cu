@@ -931,7 +931,7 @@ template <typename T, int W, int VEC>
 static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
-    if constexpr (VEC * sizeof(T) == 8) {
+    if constexpr (VEC * sizeof(T) == kBwdPacketBytes) {
 #define CC1D_GO(SI, SQ)                                                                               \
   {                                                                                                   \
     const auto kern = bwd_stream_kernel<T, W, VEC, SI, SQ, kStreamDepth, kBwdStreamThreads>;           \
@@ -965,7 +965,7 @@ static cudaError_t launch_bwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
 template <typename T>
 static cudaError_t launch_bwd_t(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   constexpr int PV = 16 / sizeof(T);
-  constexpr int SV = 8 / sizeof(T);  // the streamed kernel moves 8-byte packets
+  constexpr int SV = kBwdPacketBytes / sizeof(T);  // the streamed kernel's packets
   if (ls.layout == kLayoutStream) {
     switch (ls.width) {
       case 2: return launch_bwd_w<T, 2, SV>(a, ls, s);
@@ -989,7 +989,8 @@ template <typename T>
 static const void* bwd_kernel_ptr_t(const LaunchShape& ls) {
   constexpr int PV = 16 / sizeof(T);
   if (ls.layout == kLayoutStream) {
-    const void* k = reinterpret_cast<const void*>(bwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepth, kBwdStreamThreads>);
+    const void* k = reinterpret_cast<const void*>(
+        bwd_stream_kernel<T, 4, kBwdPacketBytes / sizeof(T), true, false, kStreamDepth, kBwdStreamThreads>);
     allow_dynamic_smem(k, ls.smem);  // so that the occupancy query sees the real limit
     return k;
   }

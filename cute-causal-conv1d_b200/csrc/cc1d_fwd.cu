@@ -670,7 +670,7 @@ template <typename T, int W, int VEC>
 static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   const bool silu = ls.silu, seq = ls.seq;
   if (ls.layout == kLayoutStream) {
-    if constexpr (VEC * sizeof(T) == 8) {
+    if constexpr (VEC * sizeof(T) == kFwdPacketBytes) {
 #define CC1D_GO_P(SI, SQ, EM, P, NT)                                                                \
   do {                                                                                              \
     const auto kern = fwd_stream_kernel<T, W, VEC, SI, SQ, P, NT, EM>;                              \
@@ -714,7 +714,7 @@ static cudaError_t launch_fwd_w(const ConvArgs& a, const LaunchShape& ls, cudaSt
 template <typename T>
 static cudaError_t launch_fwd_t(const ConvArgs& a, const LaunchShape& ls, cudaStream_t s) {
   constexpr int PV = 16 / sizeof(T);
-  constexpr int SV = 8 / sizeof(T);  // the streamed kernel moves 8-byte packets
+  constexpr int SV = kFwdPacketBytes / sizeof(T);  // the streamed kernel's packets
   if (ls.layout == kLayoutStream) {
     switch (ls.width) {
       case 2: return launch_fwd_w<T, 2, SV>(a, ls, s);
@@ -741,9 +741,10 @@ static const void* fwd_kernel_ptr_t(const LaunchShape& ls) {
   constexpr int PV = 16 / sizeof(T);
   if (ls.layout == kLayoutStream && ls.small)
     return reinterpret_cast<const void*>(
-        fwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepthFwdSmall, kFwdStreamThreadsSmall>);
+        fwd_stream_kernel<T, 4, kFwdPacketBytes / sizeof(T), true, false, kStreamDepthFwdSmall, kFwdStreamThreadsSmall>);
   if (ls.layout == kLayoutStream)
-    return reinterpret_cast<const void*>(fwd_stream_kernel<T, 4, 8 / sizeof(T), true, false, kStreamDepthFwd, kFwdStreamThreads>);
+    return reinterpret_cast<const void*>(
+        fwd_stream_kernel<T, 4, kFwdPacketBytes / sizeof(T), true, false, kStreamDepthFwd, kFwdStreamThreads>);
   if (ls.layout == kLayoutChannelLast) {
     if (ls.packet) return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, PV, true, false, 4>);
     return reinterpret_cast<const void*>(fwd_channel_last_kernel<T, 4, 1, true, false, 4>);

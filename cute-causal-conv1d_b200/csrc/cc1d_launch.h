@@ -18,9 +18,20 @@ constexpr int kStreamDepthFwd = 16;    // forward: ring slots per thread (15 row
 constexpr int kStreamDepthEmit = 8;    // forward that writes varlen states: ring slots per thread
 constexpr int kStreamThreads = 128;    // CTA size of the row-stream kernel
 constexpr int kFwdStreamThreads = 512; // CTA size of the streamed forward (one CTA per SM)
+#ifndef CC1D_FWD_PACKET
+#define CC1D_FWD_PACKET 8
+#endif
+constexpr int kFwdPacketBytes = CC1D_FWD_PACKET;  // streamed forward: bytes of channels per lane and row
 constexpr int kStreamDepthFwdSmall = 8;     // streamed forward of small problems: ring slots
 constexpr int kFwdStreamThreadsSmall = 128; // streamed forward of small problems: CTA size
-constexpr int kBwdStreamThreads = 512; // CTA size of the streamed backward (one CTA per SM at 128 registers)
+#ifndef CC1D_BWD_PACKET
+#define CC1D_BWD_PACKET 8
+#endif
+#ifndef CC1D_BWD_THREADS
+#define CC1D_BWD_THREADS 512
+#endif
+constexpr int kBwdPacketBytes = CC1D_BWD_PACKET;  // streamed backward: bytes of channels per lane and row
+constexpr int kBwdStreamThreads = CC1D_BWD_THREADS;  // CTA size of the streamed backward (one CTA per SM at 128 registers)
 constexpr int kLayoutRowStream = 3;    // (batch, dim, seqlen)-contiguous, per-lane sector stream
 constexpr int kRowDepthBwd = 4;        // row-stream backward: ring slots (32-byte sectors) per lane and tensor
 constexpr int kLayoutRowWalk = 4;      // (batch, dim, seqlen)-contiguous, lanes along the sequence
