@@ -33,7 +33,8 @@
 // launches): decode_cl/block with 4 batch rows per thread (128 CTAs, every load of a
 // thread issued together) took 5.2-6.2 us against 8.3-9.8 us with 1 row (512 CTAs, more
 // than one wave) and 6.1-6.9 us with 2; decode_ring with 2 channels and 1 row per thread
-// took 12.9 us against 18.7-22.6 us with 4 or 8 channels.
+// took 12.9-13.0 us against 18.7-22.6 us with 4 or 8 channels, and 13.0-18.1 us with 2 or
+// 4 rows of 1 or 2 channels.
 #ifndef CC1D_DECODE_ROWS
 #define CC1D_DECODE_ROWS 4  // batch rows per thread (decode_cl_kernel, decode_block_kernel)
 #endif
