@@ -220,14 +220,15 @@ Geometry plan(bool bwd, int64_t B, int64_t D, int64_t L, int width, int layout, 
 // per column) on `target` resident warps.  Estimated time ~ waves x (longest segment +
 // per-unit start-up cost, in steps); among one-wave and multi-wave splits pick the
 // smallest estimate (ties: fewer units).
-int64_t choose_units(int64_t ncol, int64_t len, int64_t max_seg, int64_t target, int64_t unit_overhead) {
+int64_t choose_units(int64_t ncol, int64_t len, int64_t max_seg, int64_t target, int64_t unit_overhead,
+                     int64_t max_waves) {
   auto cost = [&](int64_t u) {
     const int64_t q = u / ncol;  // every column has at least q segments
     return ((u + target - 1) / target) * ((len + q - 1) / q + unit_overhead);
   };
   int64_t units = std::min<int64_t>(std::max<int64_t>(target, ncol), ncol * max_seg);
   int64_t best = cost(units);
-  for (int64_t k = 1; k <= 4; ++k) {
+  for (int64_t k = 1; k <= max_waves; ++k) {
     const int64_t cands[2] = {k * target, ((k * target) / ncol) * ncol};
     for (int64_t u : cands) {
       if (u < ncol || u > ncol * max_seg) continue;
@@ -255,7 +256,7 @@ int64_t choose_units(int64_t ncol, int64_t len, int64_t max_seg, int64_t target,
 // units equals the resident warp capacity and every warp gets the same number of rows
 // (+-1 row, +-1 segment length between columns).
 Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_blocks,
-                     bool small = false) {
+                     bool small = false, bool many_waves = false) {
   Geometry g;
   std::memset(&g, 0, sizeof(g));
   g.ls.width = width;
@@ -269,7 +270,12 @@ Geometry plan_stream(bool bwd, int64_t B, int64_t D, int64_t L, int width, int e
   const int64_t min_rows = bwd ? CC1D_MIN_ROWS_BWD : CC1D_MIN_ROWS_FWD;  // shortest segment
   const int64_t max_seg = std::max<int64_t>(1, L / min_rows);
   const int64_t target = std::max<int64_t>(1, resident_blocks * warps_per_block);
-  const int64_t units = choose_units(ncol, L, max_seg, target, /*unit_overhead=*/24);
+  // Several waves of units let the SMs that draw more DRAM service take more of them.
+  // Up to 4 waves, each unit costed 24 rows of start-up; the plain forward goes up to 16
+  // waves at 2 rows (config 5 forward: 694 instead of 710-715 us; the backward measured
+  // slower with more waves: 1023 -> 1090 us at 16).
+  const int64_t units = many_waves ? choose_units(ncol, L, max_seg, target, /*unit_overhead=*/2, /*max_waves=*/16)
+                                   : choose_units(ncol, L, max_seg, target, /*unit_overhead=*/24, /*max_waves=*/4);
   g.a.nv = nv;
   g.a.ncol = ncol;
   g.a.seg_q = units / ncol;
@@ -300,7 +306,7 @@ Geometry plan_rows(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es,
   const int64_t nsteps = (L + C - 1) / C;
   const int64_t max_seg = std::max<int64_t>(1, nsteps / (bwd ? 4 : 2));
   const int64_t target = std::max<int64_t>(1, resident_blocks * (kStreamThreads / 32));
-  const int64_t units = choose_units(ncol, nsteps, max_seg, target, /*unit_overhead=*/4);
+  const int64_t units = choose_units(ncol, nsteps, max_seg, target, /*unit_overhead=*/4, /*max_waves=*/4);
   g.a.nv = D;  // one channel per lane
   g.a.ncol = ncol;
   g.a.seg_q = units / ncol;
@@ -438,7 +444,7 @@ static cc1d_status fwd_prepare(const cc1d_fwd_params* p, Geometry* out_g, bool* 
     // One CTA of 16 warps per SM with a 16-slot ring: measured faster than two CTAs per
     // SM with 8-slot rings (config 2 forward 26.5 -> 25.4 us, config 4 233 -> 228 us),
     // since each warp walks twice the rows for the same start-up.
-    g = plan_stream(false, B, D, L, W, es, (int64_t)sm_count());
+    g = plan_stream(false, B, D, L, W, es, (int64_t)sm_count(), false, /*many_waves=*/!p->seq_idx.data);
     // Small problems, whose warp units of at least the shortest segment cannot fill one
     // 16-warp CTA per SM: 128-thread CTAs with 8-slot rings, several per SM (measured on
     // (1, 2048, 2048) fp16: 4.9 instead of 5.7 us; (1, 1024, 4096): 6.2 instead of 7.1 us;
