@@ -319,7 +319,7 @@ Geometry plan_rows(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es,
   return g;
 }
 
-// Row walk ((B, D, L) contiguous, lanes along the sequence): one wave of warps, each
+// Row walk ((B, D, L) contiguous, lanes along the sequence): waves of warps, each
 // walking an equal share of the rows x steps sequence (see cc1d_rowwalk.cu).
 Geometry plan_rowwalk(bool bwd, int64_t B, int64_t D, int64_t L, int width, int es, int64_t resident_blocks) {
   Geometry g;
@@ -331,7 +331,13 @@ Geometry plan_rowwalk(bool bwd, int64_t B, int64_t D, int64_t L, int width, int 
   const int64_t steps = (L + 32 * vec - 1) / (32 * vec);
   const int64_t total = B * D * steps;
   const int64_t warps_per_block = kRowWalkThreads / 32;
-  const int64_t nw = std::max<int64_t>(1, std::min<int64_t>(resident_blocks * warps_per_block, total));
+  // The forward walks in several waves of warps when each warp keeps at least ~96 steps
+  // (up to 16): SMs that draw more DRAM service then take more warps.  Config 5 contiguous
+  // forward: 758 -> 685 us (bf16 W=4), 744 -> 669 us (fp16 W=2); (4, 4096, 8192) takes 2
+  // waves (102 -> 98 us; 16 waves there: 129 us).  The backward measured mixed and keeps one.
+  const int64_t resident_warps = resident_blocks * warps_per_block;
+  const int64_t waves = bwd ? 1 : std::max<int64_t>(1, std::min<int64_t>(16, total / (resident_warps * 96)));
+  const int64_t nw = std::max<int64_t>(1, std::min<int64_t>(waves * resident_warps, total));
   g.a.nck = steps;
   g.a.units = total;
   g.a.ncol = nw;
